@@ -1,0 +1,455 @@
+"""Decode-attention benchmark (driver contract: one JSON line from rank 0).
+
+A step is one pass of the hot path over one batch: fused RoPE + KV-page append of
+the new token of every sequence, paged GQA flash-decode over the whole context,
+and the split-K log-sum-exp merge.  Default workload = BASELINE config 2
+(Llama-3-8B decode attention: B64 Hq32 Hkv8 d128, context 4096, page 16,
+shuffled block tables, bf16).  Under torchrun with N ranks the step is
+KV-head sharded (each rank owns Hkv/N KV heads and their query heads, as the
+reference's column split of q/k/v_proj) — strong scaling, no data-path
+collective.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c2|c3|c4]
+
+``--impl reference`` times the reference's CPU path (the oracle restatement in
+``oracle/``) on the host cores with the same metric; under torchrun only rank 0
+runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+THETA = 500000.0
+
+WORKLOADS = {
+    # name: (B, Hq, Hkv, d, lengths-spec, page, scale, partition, seed, description)
+    "c2": dict(B=64, Hq=32, Hkv=8, d=128, P=16, scale=1.0, part=None, seed=1002,
+               desc="config2 Llama-3-8B decode-attention step: B64 Hq32 Hkv8 d128 ctx4096 page16 "
+                    "shuffled block tables"),
+    "c3": dict(B=256, Hq=32, Hkv=8, d=128, P=16, scale=1.0, part=None, seed=1003,
+               desc="config3 ragged batch: B256 Hq32 Hkv8 d128 ctx~U[128,32768] page16 shared pool"),
+    "c4": dict(B=4, Hq=64, Hkv=8, d=128, P=64, scale=0.5, part=4096, seed=1004,
+               desc="config4 long context split-K: B4 Hq64 Hkv8 d128 ctx131072 page64 "
+                    "4096-token partitions + LSE merge"),
+}
+
+
+def _lengths(name: str, w: dict) -> list[int]:
+    if name == "c2":
+        return [4096] * w["B"]
+    if name == "c3":
+        g = torch.Generator().manual_seed(w["seed"])
+        return torch.randint(128, 32769, (w["B"],), generator=g).tolist()
+    return [131072] * w["B"]
+
+
+def _peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return {"hbm_gbs": float(pk["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _profile_traffic(workload: str, n_gpus: int):
+    """dram bytes per decode launch from the committed ncu summary, if any."""
+    path = os.path.join(ROOT, "profiles", f"paged_decode_{workload}_traffic.json")
+    try:
+        with open(path) as f:
+            rec = json.load(f)
+        return rec.get(f"tp{n_gpus}")
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.idx)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            if self.path and os.path.exists(self.path):
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(r[1]) for r in rows]
+        mx = max(float(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle restatement of the reference's CPU decode path
+# ---------------------------------------------------------------------------
+def _cpu_unit(rng, L, G, d, dt):
+    """One (sequence, KV head) unit of a decode step for the oracle."""
+    from oracle import decode_oracle as O
+
+    q = O.round_to(rng.standard_normal((G, d), dtype=np.float32), dt)
+    k = O.round_to(rng.standard_normal((1, L, d), dtype=np.float32), dt)
+    v = O.round_to(rng.standard_normal((1, L, d), dtype=np.float32), dt)
+    cos, sin = O.build_rope_cache([L - 1], d, THETA, dt)
+    return q, k, v, cos, sin
+
+
+def _run_cpu_unit(u, dt):
+    from oracle import decode_oracle as O
+
+    q, k, v, cos, sin = u
+    qr = O.apply_rotary(q[:, None], cos, sin, dt)[:, 0]
+    return O.decode_attention(qr, k, v, dt)
+
+
+def cpu_baseline(w: dict, lengths, budget_s: float) -> dict:
+    """Time the oracle on (sequence, KV head) units of the workload for ~budget_s."""
+    dt = "bf16"
+    G, d = w["Hq"] // w["Hkv"], w["d"]
+    rng = np.random.default_rng(0)
+    L = int(lengths[len(lengths) // 2])
+    u = _cpu_unit(rng, L, G, d, dt)
+    _run_cpu_unit(u, dt)  # warm
+    n, kv_bytes = 0, 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s:
+        _run_cpu_unit(u, dt)
+        n += 1
+        kv_bytes += L * d * 2 * 2
+    el = time.perf_counter() - t0
+    return {"value": kv_bytes / el / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n} (sequence, KV head) units of ctx {L}, G={G}, d={d}, bf16 rounding "
+                      f"emulated, {el:.1f} s; numpy/OpenBLAS with {os.cpu_count()} threads"}
+
+
+def run_reference(args, w, lengths):
+    """--impl reference: the reference's CPU path (oracle port) on this host's cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    dt = "bf16"
+    G, d = w["Hq"] // w["Hkv"], w["d"]
+    rng = np.random.default_rng(0)
+    L = int(lengths[len(lengths) // 2])
+    u = _cpu_unit(rng, L, G, d, dt)
+    t0 = time.perf_counter()
+    _run_cpu_unit(u, dt)
+    t_unit = max(time.perf_counter() - t0, 1e-4)
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    units = max(1, int(budget / t_unit))
+    for _ in range(args.warmup):
+        for _ in range(units):
+            _run_cpu_unit(u, dt)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(units):
+            _run_cpu_unit(u, dt)
+    el = time.perf_counter() - t0
+    kv = units * args.steps * L * d * 2 * 2
+    value = kv / el / 1e9
+    full_kv = sum(lengths) * w["Hkv"] * d * 2 * 2
+    line = {
+        "impl": "reference", "metric": "decode-attn KV GB/s", "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3 * (full_kv / (units * L * d * 4)),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": {"workload": w["desc"], "sample_units_per_step": units},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{units} (sequence, KV head) units of ctx {L} per step "
+                                   "(oracle restatement of attention.py:56-89 + rotary.py:104-109)"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def _dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_ours(args, name, w, lengths):
+    from llm_cuda_b200 import _native as N
+    from llm_cuda_b200.kernels.decode_attention import choose_partition_tokens, paged_decode
+    from llm_cuda_b200.models.llama3 import PagedKVLayerCache, RopeTable, make_block_table
+
+    N.load()
+    world, rank, local = _dist_setup(args)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    B, Hq, Hkv, d, P = w["B"], w["Hq"], w["Hkv"], w["d"], w["P"]
+    if Hkv % world:
+        raise SystemExit(f"KV heads {Hkv} do not shard over {world} ranks")
+    hkv, hq = Hkv // world, Hq // world              # this rank's heads (TP shard)
+    dtype = torch.bfloat16
+    pages_per = [math.ceil(L / P) for L in lengths]
+    max_pages = max(pages_per)
+    kv_bytes_rank = sum(lengths) * hkv * d * 2 * 2    # K and V read per step
+    n_sets = max(1, math.ceil(3 * L2_BYTES / kv_bytes_rank)) if kv_bytes_rank < 3 * L2_BYTES else 1
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    T = w["part"] or choose_partition_tokens(lengths, hkv, hq // hkv, sms, max_pages * P)
+
+    gen = torch.Generator().manual_seed(w["seed"] + 7919 * rank)
+    gd = torch.Generator(device=dev).manual_seed(w["seed"] + rank)
+    rope = RopeTable(max_pages * P, d, THETA, dev, dtype)
+    sets = []
+    for s in range(n_sets):
+        num_pages = sum(pages_per) + 8
+        bt = make_block_table(B, pages_per, num_pages, max_pages, generator=gen)
+        cache = PagedKVLayerCache(hkv, d, max_pages * P, P, dev, dtype, batch_size=B,
+                                  num_pages=num_pages, block_table=bt)
+        cache.key_pages.normal_(generator=gd).mul_(w["scale"])
+        cache.value_pages.normal_(generator=gd).mul_(w["scale"])
+        base = torch.tensor([L - 1 for L in lengths], dtype=torch.int32, device=dev)
+        q = (torch.randn(B, hq, 1, d, device=dev, generator=gd) * w["scale"]).to(dtype)
+        k = (torch.randn(B, hkv, 1, d, device=dev, generator=gd) * w["scale"]).to(dtype)
+        v = (torch.randn(B, hkv, 1, d, device=dev, generator=gd) * w["scale"]).to(dtype)
+        sets.append(dict(cache=cache, base=base, q=q, k=k, v=v, q_rot=torch.empty_like(q),
+                         out=torch.empty(B, hq, d, device=dev, dtype=dtype)))
+    for st in sets:
+        st["cache"].host_lengths = [L - 1 for L in lengths]
+
+    def step(st, ev=None):
+        c = st["cache"]
+        c.seq_lens.copy_(st["base"])          # every step attends exactly the configured context
+        c.append_rotary(st["q"], st["k"], st["v"], rope, q_out=st["q_rot"])
+        if ev is not None:
+            ev[0].record()
+        paged_decode(st["q_rot"], c.key_pages, c.value_pages, c.block_table, c.seq_lens,
+                     partition_tokens=T, out=st["out"], workspace=c.workspace, status=c.status)
+        if ev is not None:
+            ev[1].record()
+
+    # eager warm-up (also allocates the split-K workspace before capture)
+    for st in sets:
+        step(st)
+        c = st["cache"]
+    torch.cuda.synchronize()
+    for st in sets:
+        st["cache"].check_status()
+
+    # one CUDA graph per input set
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream(dev))
+    graphs = []
+    with torch.cuda.stream(stream):
+        for st in sets:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                step(st)
+            graphs.append(g)
+    torch.cuda.current_stream(dev).wait_stream(stream)
+    torch.cuda.synchronize()
+
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup)):
+            graphs[i % n_sets].replay()
+    torch.cuda.synchronize()
+    _barrier(world)
+
+    clock = ClockSampler(dev.index if world > 1 else 0)
+    with clock:
+        # ---- timed region: K graph replays ----
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(args.steps):
+                graphs[i % n_sets].replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        _barrier(world)
+        ms = e0.elapsed_time(e1) / args.steps
+        # ---- decode-kernel duration on its launching stream (eager launches) ----
+        kreps = min(args.steps, 200)
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(kreps)]
+        with torch.cuda.stream(stream):
+            for i in range(kreps):
+                step(sets[i % n_sets], evs[i])
+        torch.cuda.synchronize()
+        k_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    clocks = clock.summary()
+    for st in sets:
+        st["cache"].check_status()
+    ms = _max_over_ranks(ms, world)
+    k_ms = _max_over_ranks(k_ms, world)
+
+    # ---- e2e through the public API with host buffers ----
+    st = sets[0]
+    c = st["cache"]
+    hq_in = torch.empty(B, hq, 1, d, dtype=dtype, pin_memory=True)
+    hk_in = torch.empty(B, hkv, 1, d, dtype=dtype, pin_memory=True)
+    hv_in = torch.empty(B, hkv, 1, d, dtype=dtype, pin_memory=True)
+    h_out = torch.empty(B, hq, 1, d, dtype=dtype, pin_memory=True)
+    hq_in.copy_(st["q"].cpu())
+    hk_in.copy_(st["k"].cpu())
+    hv_in.copy_(st["v"].cpu())
+    e2e_steps = max(10, min(args.steps, 500))
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        qd = hq_in.to(dev, non_blocking=True)
+        kd = hk_in.to(dev, non_blocking=True)
+        vd = hv_in.to(dev, non_blocking=True)
+        c.seq_lens.copy_(st["base"])
+        c.host_lengths = [L - 1 for L in lengths]
+        q_rot = c.append_rotary(qd, kd, vd, rope)
+        out = c.decode(q_rot, partition_tokens=T)
+        h_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1e3
+    _barrier(world)
+    e2e_ms = _max_over_ranks(e2e_ms, world)
+
+    total_kv = sum(lengths) * Hkv * d * 2 * 2         # all ranks together
+    value = total_kv / (ms * 1e-3) / 1e9
+    tokens_s = B / (ms * 1e-3)
+    # algorithmic bytes of one decode-kernel launch on one rank
+    alg = kv_bytes_rank + 2 * B * hq * d * 2 + sum(pages_per) * 4 + B * 4
+    achieved = alg / (k_ms * 1e-3) / 1e9
+    peaks = _peaks()
+    if rank == 0:
+        cpu = cpu_baseline(w, lengths, 15.0) if world == 1 else None
+        line = {
+            "metric": "decode-attn KV GB/s", "value": value, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V pages, q/k/v of the new token)",
+            "tokens_per_s": tokens_s,
+            "hbm_frac_step": value / world / peaks["hbm_gbs"],
+            "config": {"workload": w["desc"], "B": B, "Hq": Hq, "Hkv": Hkv, "head_dim": d,
+                       "page_size": P, "context_tokens_total": sum(lengths),
+                       "partition_tokens": T, "parallelism": f"tp{world} (KV-head sharded)",
+                       "input_sets": n_sets,
+                       "l2": f"KV per rank {kv_bytes_rank / 1e6:.0f} MB x {n_sets} rotating sets "
+                             f"> L2 126 MB (no flush needed)",
+                       "graph": "each step replayed from a CUDA graph"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": _profile_traffic(name, world),
+                         "kernel": "paged_decode_tma_kernel<128,bf16>",
+                         "kernel_ms": k_ms, "algorithmic_bytes": alg,
+                         "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": total_kv / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "ms_per_step": e2e_ms, "tokens_per_s": B / (e2e_ms * 1e-3),
+                    "h2d_bytes_per_step": (B * hq * d + 2 * B * hkv * d) * 2,
+                    "d2h_bytes_per_step": B * hq * d * 2,
+                    "path": "PagedKVLayerCache.append_rotary + .decode (ctypes C ABI), eager"},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    lengths = _lengths(args.workload, w)
+    if args.impl == "reference":
+        run_reference(args, w, lengths)
+    else:
+        run_ours(args, args.workload, w, lengths)
+
+
+if __name__ == "__main__":
+    main()

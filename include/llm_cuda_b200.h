@@ -1,0 +1,148 @@
+/*
+ * llm_cuda_b200 — C ABI of the B200 (sm_100a) decode-attention hot path.
+ *
+ * Every pointer argument is a DEVICE pointer owned by the caller; no entry point
+ * allocates device memory.  Tensors are dense row-major in the layouts given
+ * below.  Work is enqueued on `stream` and nothing synchronises the host, so the
+ * calls can be captured in a CUDA graph.  Return value: LLMC_OK (0) on success, a
+ * negative LLMC_E* code otherwise (argument validation happens on the host before
+ * any launch; `llmc_last_error_string()` holds the message, per host thread).
+ *
+ * Device-side faults are never raised by trapping: kernels OR bits into the
+ * caller's `status` word (int32 in device memory, see LLMC_STATUS_*), which the
+ * caller reads after synchronising.
+ *
+ * Paths below are files of the calvin-fei/llm-cuda project.
+ */
+#ifndef LLM_CUDA_B200_H_
+#define LLM_CUDA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* llmc_stream_t; /* == cudaStream_t */
+
+#if defined(__GNUC__)
+#define LLMC_API __attribute__((visibility("default")))
+#else
+#define LLMC_API
+#endif
+
+/* Element types (the tensor dtype of q/k/v/out, pages and cos/sin tables). */
+#define LLMC_F32 0
+#define LLMC_F16 1
+#define LLMC_BF16 2
+
+#define LLMC_OK 0
+#define LLMC_EINVAL (-1)     /* invalid argument                            */
+#define LLMC_EUNSUPPORTED (-2) /* shape/dtype combination not supported     */
+#define LLMC_ECUDA (-3)      /* CUDA runtime/driver error at launch         */
+
+/* Bits of the device status word. */
+#define LLMC_STATUS_WAIT_TIMEOUT 1
+#define LLMC_STATUS_BAD_PAGE 2
+#define LLMC_STATUS_APPEND_OVERFLOW 4
+#define LLMC_STATUS_ROPE_RANGE 8
+#define LLMC_STATUS_SEQLEN_RANGE 16
+
+/* llmc_paged_decode flags */
+#define LLMC_DECODE_FORCE_GENERIC 1 /* use the SIMT kernel even where the TMA kernel applies */
+
+/*
+ * Fused RoPE-on-new-tokens + KV-page append.
+ *
+ * Replaces, per decode step, the reference's
+ *   build_rope_cache + apply_rotary   (src/llm_cuda/models/llama3/attention.py:110-119,
+ *                                      src/llm_cuda/models/llama3/rotary.py:29-109,
+ *                                      src/llm_cuda/kernels/triton/rope.py:156-222)
+ *   PagedKVLayerCache.append          (src/llm_cuda/models/llama3/kv_cache.py:38-63)
+ * and generalises the cache to a block table over a shared page pool, batch B.
+ *
+ *   q_in   [B, Hq,  S, d]  raw query of the S new tokens (may be NULL with q_out NULL)
+ *   k_in   [B, Hkv, S, d]  raw key   (rotated before it is stored)
+ *   v_in   [B, Hkv, S, d]  value
+ *   q_out  [B, Hq,  S, d]  rotated query (NULL: not produced)
+ *   k_pages, v_pages [num_pages, Hkv, page_size, d]  the page pools (written)
+ *   block_table [B, max_pages_per_seq] int32 physical page of each logical page
+ *   seq_lens [B] int32: token s of sequence b lands at position seq_lens[b] + s;
+ *            on return seq_lens[b] has grown by S (updated on the device)
+ *   cos_tab, sin_tab [rope_max_pos, d] in the tensor dtype, rows indexed by position,
+ *            as built by build_rope_cache (rotary.py:29-71).  Both NULL: no rotation
+ *            (plain append of already-rotated k, as PagedKVLayerCache.append does).
+ * Rounding follows the reference's torch path (rotary.py:104-109): x*cos and
+ * rotate_half(x)*sin are each rounded to the dtype, then their sum.
+ */
+LLMC_API int llmc_rope_append(const void* q_in, const void* k_in, const void* v_in, void* q_out,
+                     void* k_pages, void* v_pages, const int32_t* block_table, int32_t* seq_lens,
+                     const void* cos_tab, const void* sin_tab, int B, int S, int Hq, int Hkv,
+                     int d, int page_size, int max_pages_per_seq, int num_pages, int rope_max_pos,
+                     int dtype, int32_t* status, llmc_stream_t stream);
+
+/*
+ * Workspace for split-K partials of llmc_paged_decode / llmc_lse_merge:
+ * part_o float32 [B, Hq, max_parts, d] then part_lse float32 [B, Hq, max_parts].
+ * Returns the number of BYTES of part_o (first) and, via *lse_bytes, of part_lse.
+ */
+LLMC_API size_t llmc_decode_partials_bytes(int B, int Hq, int d, int max_parts, size_t* lse_bytes);
+
+/* Number of partitions a context of `max_tokens` is split into at `partition_tokens`. */
+LLMC_API int llmc_num_partitions(int max_tokens, int partition_tokens);
+
+/*
+ * Paged GQA flash-decode: one query token per sequence against its paged K/V.
+ *
+ * Replaces triton_decode_attention / _decode_attention_kernel
+ * (src/llm_cuda/kernels/triton/decode_attention.py:47-159, 204-287) and the
+ * get_kv gather feeding it (src/llm_cuda/models/llama3/kv_cache.py:65-83): the
+ * kernel reads pages in place through the block table.  Query head h uses KV
+ * head h / (Hq / Hkv) (decode_attention.py:90-93); out = softmax(q.K^T * scale).V
+ * with out = acc / max(l, 1e-9) (decode_attention.py:154).
+ *
+ *   q   [B, Hq, d]; out [B, Hq, d] (same dtype)
+ *   k_pages, v_pages [num_pages, Hkv, page_size, d]
+ *   block_table [B, max_pages_per_seq] int32; seq_lens [B] int32 (tokens to attend)
+ *   partition_tokens: split-K partition length (multiple of 64).  Sequences with more
+ *     than one partition leave normalised partials + log2-sum-exp in part_o/part_lse
+ *     for llmc_lse_merge; single-partition sequences are written to out directly.
+ *   part_o/part_lse: see llmc_decode_partials_bytes with
+ *     max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
+ *     may be NULL when max_parts == 1.
+ *   flags: LLMC_DECODE_FORCE_GENERIC or 0.
+ * The hot kernel (bf16/fp16, d in {64,128,256}) is a persistent TMA + mbarrier
+ * pipeline with tensor-core (mma.sync) tiles, one CTA per SM; other shapes use a
+ * SIMT kernel with the same partial format.
+ */
+LLMC_API int llmc_paged_decode(const void* q, const void* k_pages, const void* v_pages,
+                      const int32_t* block_table, const int32_t* seq_lens, void* out,
+                      float* part_o, float* part_lse, int32_t* status, int B, int Hq, int Hkv,
+                      int d, int page_size, int max_pages_per_seq, int num_pages,
+                      int partition_tokens, float scale, int dtype, int flags,
+                      llmc_stream_t stream);
+
+/*
+ * Log-sum-exp merge of split-K partials into out [B, Hq, d].  For each (b, h)
+ * with n = ceil(seq_lens[b] / partition_tokens) partitions: n >= 2 merges, n == 1
+ * leaves out untouched (already written by llmc_paged_decode), n == 0 writes
+ * zeros (acc / max(l, 1e-9) with an empty context, decode_attention.py:154).
+ * No counterpart in the reference, which has no split-K; it completes
+ * triton_decode_attention's output for long contexts.
+ */
+LLMC_API int llmc_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens, void* out,
+                   int B, int Hq, int d, int max_parts, int partition_tokens, int dtype,
+                   llmc_stream_t stream);
+
+/* Message of the last failed call on this host thread ("" if none). */
+LLMC_API const char* llmc_last_error_string(void);
+
+/* Library version string. */
+LLMC_API const char* llmc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLM_CUDA_B200_H_ */

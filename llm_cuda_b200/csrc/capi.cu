@@ -1,0 +1,140 @@
+// C ABI of the decode-attention hot path (declared in include/llm_cuda_b200.h).
+//
+// Host-side argument validation happens here, before any launch; errors are
+// reported as negative return codes plus a per-thread message, never by
+// throwing across the ABI.
+#include <string>
+
+#include "common.cuh"
+
+namespace llmc {
+cudaError_t launch_rope_append(const void* q_in, const void* k_in, const void* v_in, void* q_out,
+                               void* k_pages, void* v_pages, const int32_t* bt, int32_t* seq_lens,
+                               const void* cos_tab, const void* sin_tab, int B, int S, int Hq,
+                               int Hkv, int d, int P, int max_pages, int num_pages,
+                               int rope_max_pos, int dtype, int32_t* status, cudaStream_t stream);
+cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, const int32_t* bt,
+                                const int32_t* seq_lens, void* out, float* part_o,
+                                float* part_lse, int32_t* status, int B, int Hq, int Hkv, int D,
+                                int P, int max_pages, int num_pages, int Tpart, float scale,
+                                int dtype, int flags, std::string* err, cudaStream_t stream);
+cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens,
+                             void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
+                             int dtype, cudaStream_t stream);
+}  // namespace llmc
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where, const std::string& extra = "") {
+  std::string msg = std::string(where) + ": " + cudaGetErrorString(e);
+  if (!extra.empty()) msg += " (" + extra + ")";
+  return fail(LLMC_ECUDA, msg);
+}
+
+bool valid_dtype(int dt) { return dt == LLMC_F32 || dt == LLMC_F16 || dt == LLMC_BF16; }
+}  // namespace
+
+extern "C" {
+
+const char* llmc_last_error_string(void) { return g_last_error.c_str(); }
+
+const char* llmc_version(void) { return "llm_cuda_b200 0.1.0 (sm_100a)"; }
+
+int llmc_num_partitions(int max_tokens, int partition_tokens) {
+  if (max_tokens <= 0 || partition_tokens <= 0) return 0;
+  return (max_tokens + partition_tokens - 1) / partition_tokens;
+}
+
+size_t llmc_decode_partials_bytes(int B, int Hq, int d, int max_parts, size_t* lse_bytes) {
+  const size_t rows = (size_t)(B > 0 ? B : 0) * (Hq > 0 ? Hq : 0) * (max_parts > 0 ? max_parts : 0);
+  if (lse_bytes) *lse_bytes = rows * sizeof(float);
+  return rows * (size_t)(d > 0 ? d : 0) * sizeof(float);
+}
+
+int llmc_rope_append(const void* q_in, const void* k_in, const void* v_in, void* q_out,
+                     void* k_pages, void* v_pages, const int32_t* block_table, int32_t* seq_lens,
+                     const void* cos_tab, const void* sin_tab, int B, int S, int Hq, int Hkv,
+                     int d, int page_size, int max_pages_per_seq, int num_pages, int rope_max_pos,
+                     int dtype, int32_t* status, llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_rope_append: unknown dtype");
+  if (B < 0 || S < 0 || Hkv <= 0 || Hq < 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
+      num_pages <= 0)
+    return fail(LLMC_EINVAL, "llmc_rope_append: sizes must be positive");
+  if (d % 2) return fail(LLMC_EINVAL, "llmc_rope_append: head_dim must be even (rotate_half)");
+  if ((cos_tab == nullptr) != (sin_tab == nullptr))
+    return fail(LLMC_EINVAL, "llmc_rope_append: cos_tab and sin_tab must both be set or both NULL");
+  if (cos_tab && rope_max_pos <= 0)
+    return fail(LLMC_EINVAL, "llmc_rope_append: rope_max_pos must be positive with a table");
+  if ((q_out == nullptr) != (q_in == nullptr))
+    return fail(LLMC_EINVAL, "llmc_rope_append: q_in and q_out must both be set or both NULL");
+  if (!k_in || !v_in || !k_pages || !v_pages || !block_table || !seq_lens || !status)
+    return fail(LLMC_EINVAL, "llmc_rope_append: NULL pointer argument");
+  if (B == 0 || S == 0) return LLMC_OK;
+  cudaError_t e = llmc::launch_rope_append(q_in, k_in, v_in, q_out, k_pages, v_pages, block_table,
+                                           seq_lens, cos_tab, sin_tab, B, S, Hq, Hkv, d,
+                                           page_size, max_pages_per_seq, num_pages, rope_max_pos,
+                                           dtype, status, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_rope_append");
+  return LLMC_OK;
+}
+
+int llmc_paged_decode(const void* q, const void* k_pages, const void* v_pages,
+                      const int32_t* block_table, const int32_t* seq_lens, void* out,
+                      float* part_o, float* part_lse, int32_t* status, int B, int Hq, int Hkv,
+                      int d, int page_size, int max_pages_per_seq, int num_pages,
+                      int partition_tokens, float scale, int dtype, int flags,
+                      llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_paged_decode: unknown dtype");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
+      num_pages <= 0 || partition_tokens <= 0)
+    return fail(LLMC_EINVAL, "llmc_paged_decode: sizes must be positive");
+  if (Hq % Hkv) return fail(LLMC_EINVAL, "llmc_paged_decode: Hq must be a multiple of Hkv");
+  if (d > 256) return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode: head_dim > 256");
+  if (partition_tokens % 64)
+    return fail(LLMC_EINVAL, "llmc_paged_decode: partition_tokens must be a multiple of 64");
+  if ((long long)Hq / Hkv * d > 16384)
+    return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode: (Hq/Hkv) * head_dim > 16384");
+  if ((long long)num_pages * Hkv * page_size >= (1ll << 31))
+    return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode: page pool rows exceed 2^31");
+  if (!q || !k_pages || !v_pages || !block_table || !seq_lens || !out || !status)
+    return fail(LLMC_EINVAL, "llmc_paged_decode: NULL pointer argument");
+  const int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
+  if (max_parts > 1 && (!part_o || !part_lse))
+    return fail(LLMC_EINVAL,
+                "llmc_paged_decode: part_o/part_lse are required when a sequence can span "
+                "more than one partition");
+  std::string err;
+  cudaError_t e = llmc::launch_paged_decode(q, k_pages, v_pages, block_table, seq_lens, out,
+                                            part_o, part_lse, status, B, Hq, Hkv, d, page_size,
+                                            max_pages_per_seq, num_pages, partition_tokens, scale,
+                                            dtype, flags, &err, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_paged_decode", err);
+  return LLMC_OK;
+}
+
+int llmc_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens, void* out,
+                   int B, int Hq, int d, int max_parts, int partition_tokens, int dtype,
+                   llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_lse_merge: unknown dtype");
+  if (B < 0 || Hq <= 0 || d <= 0 || max_parts <= 0 || partition_tokens <= 0)
+    return fail(LLMC_EINVAL, "llmc_lse_merge: sizes must be positive");
+  if (!seq_lens || !out) return fail(LLMC_EINVAL, "llmc_lse_merge: NULL pointer argument");
+  if (max_parts > 1 && (!part_o || !part_lse))
+    return fail(LLMC_EINVAL, "llmc_lse_merge: NULL partials with max_parts > 1");
+  cudaError_t e = llmc::launch_lse_merge(part_o, part_lse, seq_lens, out, B, Hq, d, max_parts,
+                                         partition_tokens, max_parts * partition_tokens, dtype,
+                                         (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_lse_merge");
+  return LLMC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,748 @@
+// Paged GQA flash-decode for sm_100a + the split-K log-sum-exp merge.
+//
+// Work item = (sequence b, partition of `T` tokens, KV head, group of <= 8 query
+// heads).  All query heads of a KV head (the GQA group) sit in one CTA, so every
+// K/V byte is read from HBM once per step.
+//
+// Fast kernel (bf16/fp16, head_dim 64/128/256): persistent, one CTA per SM,
+// walking work items round-robin.  The last warp is the producer: it reads the block
+// table and issues TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) loads of the
+// K and V page rows of each 64-token stage into a ring of shared-memory slots,
+// signalling per-slot "full" mbarriers with transaction bytes.  Warps 0-2 are
+// consumers: stage s is processed by warp s % 3, which
+//   S^T[16 tok x 8 heads] = K[16 x d] . Q^T      (mma.sync m16n8k16, K via ldmatrix)
+//   online softmax per head in the log2 domain   (warp shuffles across the 8 rows)
+//   O^T[d x 8 heads]     += V^T[d x 16] . P^T    (V via ldmatrix.trans, P via movmatrix)
+// and releases the slot on its "empty" mbarrier.  At the end of an item the three
+// consumers combine (m, l, O) through shared memory and write either the final
+// output (single-partition sequence) or a normalised partial + log2-sum-exp.
+//
+// Generic kernel (any dtype incl. fp32, any head_dim <= 256, any page size):
+// one CTA per item, SIMT dot products, exact expf; same partial format.
+//
+// Merge kernel: out = sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M).
+#include <math.h>
+
+#include <string>
+
+#include "common.cuh"
+
+namespace llmc {
+
+// ---------------------------------------------------------------------------
+// Fast kernel
+// ---------------------------------------------------------------------------
+namespace fast {
+
+constexpr int kStageTok = 64;          // tokens per pipeline stage
+// Consumer warps.  Stage st lives in ring slot st % nstages and is consumed by
+// warp st % kConsumers; nstages is a multiple of kConsumers, so every slot is
+// always consumed by the same warp.  That keeps each mbarrier wait at most one
+// phase behind the barrier, which parity waits require: were two warps to share
+// a slot, a warp could wait on a phase parity that an earlier round already
+// completed and run ahead on stale data.
+constexpr int kConsumers = 3;
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kMaxStages = 12;
+constexpr int kRowBytes = 128;         // one swizzle row = 64 bf16/fp16 elements
+
+struct Params {
+  const void* q;
+  void* out;
+  float* part_o;
+  float* part_lse;
+  const int32_t* block_table;
+  const int32_t* seq_lens;
+  int32_t* status;
+  int B, Hq, Hkv, G, HG, P, max_pages, T, max_parts, num_pages, nstages;
+  float scale_log2;  // softmax scale * log2(e)
+};
+
+// Byte offset of (row, 16-byte chunk) inside a 128B-swizzled region whose base is
+// 1024-byte aligned (TMA SWIZZLE_128B: chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  return row * kRowBytes + ((chunk ^ (row & 7)) << 4);
+}
+
+struct Item {
+  int b, part, kvh, hg, t0, t1;
+};
+
+__device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int Hkv, int HG,
+                                            const int32_t* seq_lens, int T, int cap) {
+  // prefix[b] = number of items before sequence b; binary search for b.
+  int lo = 0, hi = B;  // prefix[lo] <= i < prefix[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= i) lo = mid; else hi = mid;
+  }
+  Item it;
+  it.b = lo;
+  const int r = i - prefix[lo];
+  const int per_part = Hkv * HG;
+  it.part = r / per_part;
+  const int kh = r - it.part * per_part;
+  it.kvh = kh / HG;
+  it.hg = kh - it.kvh * HG;
+  const int L = min(seq_lens[it.b], cap);
+  it.t0 = it.part * T;
+  it.t1 = min(L, it.t0 + T);
+  return it;
+}
+
+template <int D, typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                        const __grid_constant__ CUtensorMap tmap_v, const Params p) {
+  constexpr int HALVES = D / 64;
+  constexpr int KC = D / 16;                    // k-chunks of 16 along head_dim
+  constexpr int HALF_BYTES = kStageTok * kRowBytes;          // 8 KB
+  constexpr int KV_BYTES = HALVES * HALF_BYTES;              // K (or V) of one stage
+  constexpr int STAGE_BYTES = 2 * KV_BYTES;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  const int nst = p.nstages;
+  uint8_t* ring = smem;
+  float* comb_o = reinterpret_cast<float*>(smem + nst * STAGE_BYTES);  // [kConsumers][D][8]
+  float* comb_m = comb_o + kConsumers * D * 8;                        // [kConsumers][8]
+  float* comb_l = comb_m + kConsumers * 8;                            // [kConsumers][8]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(comb_l + kConsumers * 8);
+  uint64_t* empty_bar = full_bar + kMaxStages;
+  int* prefix = reinterpret_cast<int*>(empty_bar + kMaxStages);       // [B + 1]
+  volatile int* abort_flag = prefix + p.B + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- set-up: barriers + per-sequence item prefix sums (producer warp scans) ----
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < nst; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kConsumers) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmap_k);
+      prefetch_tensormap(&tmap_v);
+    }
+    const int per = (p.B + 31) / 32;
+    const int lo = min(p.B, lane * per), hi = min(p.B, lo + per);
+    const int per_part = p.Hkv * p.HG;
+    int sum = 0;
+    for (int b = lo; b < hi; ++b) {
+      int L = p.seq_lens[b];
+      const int cap = p.max_pages * p.P;
+      if (L > cap) {
+        atomicOr(p.status, kStatusSeqLenRange);
+        L = cap;
+      }
+      sum += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    int run = incl - sum;
+    for (int b = lo; b < hi; ++b) {
+      prefix[b] = run;
+      int L = min(p.seq_lens[b], p.max_pages * p.P);
+      run += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
+    }
+    if (lane == 31) prefix[p.B] = incl;
+  }
+  __syncthreads();
+  const int total_items = prefix[p.B];
+
+  if (warp == kConsumers) {
+    // ======================= producer warp =======================
+    uint32_t stage = 0;
+    for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
+      const Item it = decode_item(i, prefix, p.B, p.Hkv, p.HG, p.seq_lens, p.T, p.max_pages * p.P);
+      const int32_t* bt = p.block_table + (size_t)it.b * p.max_pages;
+      const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
+      for (int s = 0; s < nstage; ++s, ++stage) {
+        const int slot = stage % nst;
+        const uint32_t round = stage / nst;
+        const int tok0 = it.t0 + s * kStageTok;
+        // Pages touched by this stage and the box (rows) loaded from each.
+        int npg, rows, first_page, row0;
+        if (p.P >= kStageTok) {
+          npg = 1; rows = kStageTok; first_page = tok0 / p.P; row0 = tok0 - first_page * p.P;
+        } else {
+          first_page = tok0 / p.P; row0 = 0; rows = p.P;
+          npg = min(kStageTok / p.P, (it.t1 - first_page * p.P + p.P - 1) / p.P);
+        }
+        // Lane j < npg fetches page id j of this stage.
+        int page = 0;
+        bool page_ok = true;
+        if (lane < npg) {
+          page = bt[first_page + lane];
+          if (page < 0 || page >= p.num_pages) {
+            atomicOr(p.status, kStatusBadPage);
+            page_ok = false;
+          }
+        }
+        const unsigned okmask = __ballot_sync(0xffffffffu, lane < npg && page_ok);
+        const int nboxes = __popc(okmask) * HALVES * 2;
+        const uint32_t bytes = nboxes * rows * kRowBytes;
+        const uint32_t fb = smem_u32(&full_bar[slot]);
+        mbar_wait_bounded(smem_u32(&empty_bar[slot]), (round & 1u) ^ 1u, abort_flag, p.status);
+        if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
+        __syncwarp();
+        if (!*abort_flag && lane < npg && page_ok) {
+          const int row = (page * p.Hkv + it.kvh) * p.P + row0;
+          const uint32_t kdst = smem_u32(ring + slot * STAGE_BYTES) + lane * rows * kRowBytes;
+#pragma unroll
+          for (int h = 0; h < HALVES; ++h) {
+            tma_load_2d(kdst + h * HALF_BYTES, &tmap_k, h * 64, row, fb);
+            tma_load_2d(kdst + KV_BYTES + h * HALF_BYTES, &tmap_v, h * 64, row, fb);
+          }
+        }
+      }
+    }
+    // Drain: wait (bounded) for the last load issued into every slot.
+    if (lane == 0) {
+      const uint32_t n = stage < (uint32_t)nst ? stage : (uint32_t)nst;
+      for (uint32_t k = 0; k < n; ++k) {
+        const uint32_t st = stage - 1 - k;
+        mbar_wait_bounded(smem_u32(&full_bar[st % nst]), (st / nst) & 1u, abort_flag, p.status);
+      }
+    }
+    return;
+  }
+
+  // ======================= consumer warps =======================
+  const int g = lane >> 2;   // fragment row group
+  const int c = lane & 3;    // fragment column pair
+  const T* qbase = reinterpret_cast<const T*>(p.q);
+  uint32_t stage = 0;
+  for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
+    const Item it = decode_item(i, prefix, p.B, p.Hkv, p.HG, p.seq_lens, p.T, p.max_pages * p.P);
+    const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
+    const int ghead = it.hg * 8 + g;           // head within the GQA group (column n = g)
+    const bool head_ok = ghead < p.G;
+    const int hq_n = it.kvh * p.G + ghead;
+
+    // Q^T as the B operand (k = head_dim, n = head): b0b1 = q[n][16kc+2c..], b2b3 = +8.
+    uint32_t qf[KC][2];
+    {
+      const T* qrow = qbase + ((size_t)it.b * p.Hq + (head_ok ? hq_n : 0)) * D;
+#pragma unroll
+      for (int kc = 0; kc < KC; ++kc) {
+        qf[kc][0] = head_ok ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c) : 0u;
+        qf[kc][1] = head_ok ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c + 8) : 0u;
+      }
+    }
+    float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
+    float l_run[2] = {0.f, 0.f};               // per-thread partial sums
+    float o[KC][4];                            // O^T fragments: rows d, cols heads
+#pragma unroll
+    for (int mt = 0; mt < KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+
+    for (int s = 0; s < nstage; ++s, ++stage) {
+      if ((int)(stage % kConsumers) != warp) continue;
+      const int slot = stage % nst;
+      const uint32_t round = stage / nst;
+      mbar_wait_bounded(smem_u32(&full_bar[slot]), round & 1u, abort_flag, p.status);
+      const int tok0 = it.t0 + s * kStageTok;
+      const int nvalid = min(kStageTok, it.t1 - tok0);
+      uint8_t* kst = ring + slot * STAGE_BYTES;
+      uint8_t* vst = kst + KV_BYTES;
+      if (nvalid < kStageTok) {
+        // Rows past the context may hold stale or never-written bytes (possibly
+        // NaN); probabilities there are 0 but 0*NaN is NaN, so zero V's rows.
+        const int nchunk = (kStageTok - nvalid) * 8;
+#pragma unroll
+        for (int h = 0; h < HALVES; ++h)
+          for (int k = lane; k < nchunk; k += 32)
+            *reinterpret_cast<uint4*>(vst + h * HALF_BYTES + nvalid * kRowBytes + k * 16) =
+                make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      const uint32_t kaddr = smem_u32(kst);
+      const uint32_t vaddr = smem_u32(vst);
+      const int ntiles = (nvalid + 15) >> 4;
+
+      // ---- S^T = K . Q^T for up to 4 tiles of 16 tokens ----
+      float sacc[4][4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
+        if (t < ntiles) {
+          const int row = t * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+          for (int kc = 0; kc < KC; ++kc) {
+            const int d0 = kc * 16 + (lane >> 4) * 8;
+            const uint32_t addr = kaddr + (d0 >> 6) * HALF_BYTES + swz(row, (d0 & 63) >> 3);
+            uint32_t a[4];
+            ldsm_x4(addr, a[0], a[1], a[2], a[3]);
+            Mma<T>::run(sacc[t], a, qf[kc][0], qf[kc][1]);
+          }
+        }
+      }
+      // ---- online softmax (log2 domain); c0/c2 -> head 2c, c1/c3 -> head 2c+1 ----
+      float mloc[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int tok = t * 16 + g + ((r >> 1) << 3);
+          const float v = (tok < nvalid) ? sacc[t][r] * p.scale_log2 : -INFINITY;
+          sacc[t][r] = v;
+          mloc[r & 1] = fmaxf(mloc[r & 1], v);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 4));
+        mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 8));
+        mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 16));
+      }
+      float alpha[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const float mn = fmaxf(m_run[j], mloc[j]);
+        alpha[j] = exp2f(m_run[j] - mn);   // m_run = -inf -> 0
+        m_run[j] = mn;
+        l_run[j] *= alpha[j];
+      }
+#pragma unroll
+      for (int mt = 0; mt < KC; ++mt) {
+        o[mt][0] *= alpha[0]; o[mt][1] *= alpha[1];
+        o[mt][2] *= alpha[0]; o[mt][3] *= alpha[1];
+      }
+      // ---- P, then O^T += V^T . P^T ----
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (t < ntiles) {
+          float pr[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            pr[r] = exp2f(sacc[t][r] - m_run[r & 1]);
+            l_run[r & 1] += pr[r];
+          }
+          // S^T fragment rows are tokens, columns heads; the B operand needs
+          // (k = token, n = head): transpose each 8x8 block in registers.
+          const uint32_t b0 = movmatrix_trans(Mma<T>::pack(pr[0], pr[1]));
+          const uint32_t b1 = movmatrix_trans(Mma<T>::pack(pr[2], pr[3]));
+          const int vrow = t * 16 + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+          for (int mt = 0; mt < KC; ++mt) {
+            const int d0 = mt * 16 + ((lane >> 3) & 1) * 8;
+            const uint32_t addr = vaddr + (d0 >> 6) * HALF_BYTES + swz(vrow, (d0 & 63) >> 3);
+            uint32_t a[4];
+            ldsm_x4_trans(addr, a[0], a[1], a[2], a[3]);
+            Mma<T>::run(o[mt], a, b0, b1);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
+    }
+
+    // ---- item epilogue: combine the consumer warps ----
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
+      l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
+      l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
+    }
+    float* my_o = comb_o + warp * D * 8;
+#pragma unroll
+    for (int mt = 0; mt < KC; ++mt) {
+      const int d0 = mt * 16 + g;
+      my_o[d0 * 8 + 2 * c] = o[mt][0];
+      my_o[d0 * 8 + 2 * c + 1] = o[mt][1];
+      my_o[(d0 + 8) * 8 + 2 * c] = o[mt][2];
+      my_o[(d0 + 8) * 8 + 2 * c + 1] = o[mt][3];
+    }
+    if (g == 0) {
+      comb_m[warp * 8 + 2 * c] = m_run[0];
+      comb_m[warp * 8 + 2 * c + 1] = m_run[1];
+      comb_l[warp * 8 + 2 * c] = l_run[0];
+      comb_l[warp * 8 + 2 * c + 1] = l_run[1];
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    const int nh = min(8, p.G - it.hg * 8);
+    const bool single = min(p.seq_lens[it.b], p.max_pages * p.P) <= p.T;  // one partition
+    for (int idx = threadIdx.x; idx < nh * D; idx += kConsumers * 32) {
+      const int n = idx / D;
+      const int d = idx - n * D;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, comb_m[w * 8 + n]);
+      float lsum = 0.f, acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) {
+        const float sc = exp2f(comb_m[w * 8 + n] - M);   // warp without tokens: 0
+        lsum += comb_l[w * 8 + n] * sc;
+        acc += comb_o[(w * D + d) * 8 + n] * sc;
+      }
+      const int hq = it.kvh * p.G + it.hg * 8 + n;
+      const size_t row = (size_t)it.b * p.Hq + hq;
+      if (single) {
+        reinterpret_cast<T*>(p.out)[row * D + d] = from_f32<T>(acc / fmaxf(lsum, 1e-9f));
+      } else {
+        const size_t pi = row * p.max_parts + it.part;
+        p.part_o[pi * D + d] = acc / lsum;
+        if (d == 0) p.part_lse[pi] = M + log2f(lsum);
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+  }
+}
+
+}  // namespace fast
+
+// ---------------------------------------------------------------------------
+// Generic SIMT kernel: one CTA per (partition, kv head, sequence).
+// ---------------------------------------------------------------------------
+namespace generic {
+
+constexpr int kChunk = 64;
+constexpr int kThreads = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+paged_decode_simt_kernel(const T* __restrict__ q, const T* __restrict__ k_pages,
+                         const T* __restrict__ v_pages, const int32_t* __restrict__ block_table,
+                         const int32_t* __restrict__ seq_lens, T* __restrict__ out,
+                         float* __restrict__ part_o, float* __restrict__ part_lse,
+                         int32_t* __restrict__ status, int Hq, int Hkv, int D, int P,
+                         int max_pages, int num_pages, int Tpart, int max_parts, float scale) {
+  extern __shared__ float sm[];
+  const int part = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hkv;
+  int L = seq_lens[b];
+  if (L > max_pages * P) {
+    if (threadIdx.x == 0 && part == 0 && kvh == 0) atomicOr(status, kStatusSeqLenRange);
+    L = max_pages * P;
+  }
+  const int t0 = part * Tpart;
+  if (t0 >= L) return;
+  const int t1 = min(L, t0 + Tpart);
+  const int nparts = (L + Tpart - 1) / Tpart;
+
+  float* qs = sm;                    // [G][D]
+  float* acc = qs + G * D;           // [G][D]
+  float* sc = acc + G * D;           // [G][kChunk]
+  float* mrun = sc + G * kChunk;     // [G]
+  float* lrun = mrun + G;            // [G]
+  float* alph = lrun + G;            // [G]
+  __shared__ int pages[kChunk];
+
+  for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
+    const int n = idx / D, d = idx - n * D;
+    qs[idx] = to_f32(q[((size_t)b * Hq + kvh * G + n) * D + d]);
+    acc[idx] = 0.f;
+  }
+  for (int n = threadIdx.x; n < G; n += kThreads) {
+    mrun[n] = -INFINITY;
+    lrun[n] = 0.f;
+  }
+  const int32_t* bt = block_table + (size_t)b * max_pages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  for (int c0 = t0; c0 < t1; c0 += kChunk) {
+    const int nt = min(kChunk, t1 - c0);
+    __syncthreads();
+    for (int t = threadIdx.x; t < nt; t += kThreads) {
+      int pg = bt[(c0 + t) / P];
+      if (pg < 0 || pg >= num_pages) {
+        atomicOr(status, kStatusBadPage);
+        pg = -1;
+      }
+      pages[t] = pg;
+    }
+    __syncthreads();
+    // scores s = (q . k) * scale, fp32 accumulation in head_dim order
+    for (int idx = threadIdx.x; idx < G * nt; idx += kThreads) {
+      const int n = idx / nt, t = idx - n * nt;
+      const int pos = c0 + t;
+      float s = -INFINITY;
+      if (pages[t] >= 0) {
+        const T* kr = k_pages + (((size_t)pages[t] * Hkv + kvh) * P + (pos % P)) * D;
+        const float* qr = qs + n * D;
+        float a = 0.f;
+        for (int d = 0; d < D; ++d) a = fmaf(qr[d], to_f32(kr[d]), a);
+        s = a * scale;
+      }
+      sc[n * kChunk + t] = s;
+    }
+    __syncthreads();
+    // online softmax update per head (warp w: heads w, w+4, ...)
+    for (int n = warp; n < G; n += kThreads / 32) {
+      float mx = -INFINITY;
+      for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, sc[n * kChunk + t]);
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mold = mrun[n];
+      const float mnew = fmaxf(mold, mx);
+      float sum = 0.f;
+      for (int t = lane; t < nt; t += 32) {
+        const float e = (mnew == -INFINITY) ? 0.f : expf(sc[n * kChunk + t] - mnew);
+        sc[n * kChunk + t] = e;
+        sum += e;
+      }
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      __syncwarp();
+      if (lane == 0) {
+        const float a = (mold == -INFINITY) ? 0.f : expf(mold - mnew);
+        alph[n] = a;
+        lrun[n] = lrun[n] * a + sum;
+        mrun[n] = mnew;
+      }
+    }
+    __syncthreads();
+    // acc = acc * alpha + P . V   (threads over (head, d); V reads coalesced along d)
+    for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
+      const int n = idx / D, d = idx - n * D;
+      float a = acc[idx] * alph[n];
+      for (int t = 0; t < nt; ++t) {
+        if (pages[t] < 0) continue;
+        const int pos = c0 + t;
+        const T* vr = v_pages + (((size_t)pages[t] * Hkv + kvh) * P + (pos % P)) * D;
+        a = fmaf(sc[n * kChunk + t], to_f32(vr[d]), a);
+      }
+      acc[idx] = a;
+    }
+  }
+  __syncthreads();
+  const float kLog2e = 1.4426950408889634f;
+  for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
+    const int n = idx / D, d = idx - n * D;
+    const size_t row = (size_t)b * Hq + kvh * G + n;
+    if (nparts == 1) {
+      out[row * D + d] = from_f32<T>(acc[idx] / fmaxf(lrun[n], 1e-9f));
+    } else {
+      const size_t pi = row * max_parts + part;
+      part_o[pi * D + d] = acc[idx] / lrun[n];
+      if (d == 0) part_lse[pi] = mrun[n] * kLog2e + log2f(lrun[n]);
+    }
+  }
+}
+
+size_t smem_bytes(int G, int D) {
+  return sizeof(float) * (size_t)(2 * G * D + G * kChunk + 3 * G);
+}
+
+}  // namespace generic
+
+// ---------------------------------------------------------------------------
+// Log-sum-exp merge: one CTA per (b, h); threads over head_dim.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(128)
+lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                 const int32_t* __restrict__ seq_lens, T* __restrict__ out, int Hq, int D,
+                 int max_parts, int Tpart, int cap) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int L = min(seq_lens[b], cap);
+  const int n = L > 0 ? (L + Tpart - 1) / Tpart : 0;
+  const size_t row = (size_t)b * Hq + h;
+  if (n == 1) return;  // written directly by the decode kernel
+  if (n == 0) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) out[row * D + d] = from_f32<T>(0.f);
+    return;
+  }
+  const float* lse = part_lse + row * max_parts;
+  float M = -INFINITY;
+  for (int i = 0; i < n; ++i) M = fmaxf(M, lse[i]);
+  float wsum = 0.f;
+  for (int i = 0; i < n; ++i) wsum += exp2f(lse[i] - M);
+  const float inv = 1.f / wsum;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float a = 0.f;
+    for (int i = 0; i < n; ++i) a = fmaf(exp2f(lse[i] - M), part_o[(row * max_parts + i) * D + d], a);
+    out[row * D + d] = from_f32<T>(a * inv);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host launchers
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D view of a page pool [num_pages * Hkv * P rows, D cols], box {64 cols, rows}.
+static bool encode_pool_map(CUtensorMap* map, const void* base, long long nrows, int D, int rows,
+                            std::string* err) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) {
+    *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
+    return false;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)nrows};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r);
+    return false;
+  }
+  return true;
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem_optin = 0;
+};
+
+static DeviceInfo device_info() {
+  static DeviceInfo cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev].sms == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin,
+                           dev);
+  }
+  return cache[dev];
+}
+
+bool fast_path_applies(int dtype, int D, int P, int max_pages, int Tpart, int B,
+                       const void* q, const void* kp, const void* vp) {
+  if (dtype != LLMC_BF16 && dtype != LLMC_F16) return false;
+  if (D != 64 && D != 128 && D != 256) return false;
+  if (Tpart % fast::kStageTok) return false;
+  const bool p_ok = (P == 8 || P == 16 || P == 32 || P == 64) || (P % fast::kStageTok == 0) ||
+                    max_pages == 1;
+  if (!p_ok) return false;
+  if (B > 8192) return false;
+  auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
+  return al(q) && al(kp) && al(vp);
+}
+
+template <int D, typename T>
+static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const void* vp,
+                                 long long nrows, std::string* err, cudaStream_t stream) {
+  fast::Params p = p0;
+  const int rows = p.P >= fast::kStageTok ? fast::kStageTok : p.P;
+  CUtensorMap mk, mv;
+  if (!encode_pool_map(&mk, kp, nrows, D, rows, err) ||
+      !encode_pool_map(&mv, vp, nrows, D, rows, err))
+    return cudaErrorInvalidValue;
+  const DeviceInfo di = device_info();
+  constexpr int STAGE_BYTES = 2 * (D / 64) * fast::kStageTok * fast::kRowBytes;
+  const size_t fixed = 1024 /*align*/ + sizeof(float) * (fast::kConsumers * D * 8 + 16 * fast::kConsumers) +
+                       2 * fast::kMaxStages * sizeof(uint64_t) + sizeof(int) * (p.B + 2) + 64;
+  const size_t budget = (size_t)di.max_smem_optin;
+  int nst = (int)((budget - fixed) / STAGE_BYTES);
+  if (nst > fast::kMaxStages) nst = fast::kMaxStages;
+  nst -= nst % fast::kConsumers;  // each slot is owned by one consumer warp
+  if (nst < fast::kConsumers) {
+    *err = "not enough shared memory for the decode pipeline";
+    return cudaErrorInvalidValue;
+  }
+  p.nstages = nst;
+  const size_t smem = fixed + (size_t)nst * STAGE_BYTES;
+  auto kern = fast::paged_decode_tma_kernel<D, T>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  long long upper = (long long)p.B * p.max_parts * p.Hkv * p.HG;
+  int grid = di.sms;
+  if (upper < grid) grid = (int)(upper > 0 ? upper : 1);
+  kern<<<grid, fast::kThreads, smem, stream>>>(mk, mv, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, const int32_t* bt,
+                                const int32_t* seq_lens, void* out, float* part_o,
+                                float* part_lse, int32_t* status, int B, int Hq, int Hkv, int D,
+                                int P, int max_pages, int num_pages, int Tpart, float scale,
+                                int dtype, int flags, std::string* err, cudaStream_t stream) {
+  const int G = Hq / Hkv;
+  const int max_parts = (max_pages * P + Tpart - 1) / Tpart;
+  if (B == 0) return cudaSuccess;
+  if (!(flags & LLMC_DECODE_FORCE_GENERIC) &&
+      fast_path_applies(dtype, D, P, max_pages, Tpart, B, q, kp, vp)) {
+    fast::Params p;
+    p.q = q; p.out = out; p.part_o = part_o; p.part_lse = part_lse; p.block_table = bt;
+    p.seq_lens = seq_lens; p.status = status;
+    p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
+    p.max_pages = max_pages; p.T = Tpart; p.max_parts = max_parts; p.num_pages = num_pages;
+    p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
+    const long long nrows = (long long)num_pages * Hkv * P;
+    if (dtype == LLMC_BF16) {
+      if (D == 64) return launch_fast_t<64, __nv_bfloat16>(p, kp, vp, nrows, err, stream);
+      if (D == 128) return launch_fast_t<128, __nv_bfloat16>(p, kp, vp, nrows, err, stream);
+      return launch_fast_t<256, __nv_bfloat16>(p, kp, vp, nrows, err, stream);
+    } else {
+      if (D == 64) return launch_fast_t<64, __half>(p, kp, vp, nrows, err, stream);
+      if (D == 128) return launch_fast_t<128, __half>(p, kp, vp, nrows, err, stream);
+      return launch_fast_t<256, __half>(p, kp, vp, nrows, err, stream);
+    }
+  }
+  // generic SIMT path
+  const size_t smem = generic::smem_bytes(G, D);
+  dim3 grid(max_parts, Hkv, B);
+  if (max_parts > 65535 * 1024 || Hkv > 65535 || B > 65535) {
+    *err = "grid too large for the generic decode kernel";
+    return cudaErrorInvalidValue;
+  }
+#define LLMC_GEN(TT)                                                                          \
+  do {                                                                                        \
+    auto k = generic::paged_decode_simt_kernel<TT>;                                           \
+    if (smem > 48 * 1024) {                                                                   \
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                           (int)smem);                                        \
+      if (e != cudaSuccess) return e;                                                         \
+    }                                                                                         \
+    k<<<grid, generic::kThreads, smem, stream>>>((const TT*)q, (const TT*)kp, (const TT*)vp,  \
+                                                 bt, seq_lens, (TT*)out, part_o, part_lse,    \
+                                                 status, Hq, Hkv, D, P, max_pages, num_pages, \
+                                                 Tpart, max_parts, scale);                    \
+  } while (0)
+  if (dtype == LLMC_F32) LLMC_GEN(float);
+  else if (dtype == LLMC_F16) LLMC_GEN(__half);
+  else LLMC_GEN(__nv_bfloat16);
+#undef LLMC_GEN
+  return cudaGetLastError();
+}
+
+cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens,
+                             void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
+                             int dtype, cudaStream_t stream) {
+  if (B == 0 || Hq == 0) return cudaSuccess;
+  dim3 grid(Hq, B);
+  if (dtype == LLMC_F32)
+    lse_merge_kernel<float><<<grid, 128, 0, stream>>>(part_o, part_lse, seq_lens, (float*)out, Hq,
+                                                      D, max_parts, Tpart, cap);
+  else if (dtype == LLMC_F16)
+    lse_merge_kernel<__half><<<grid, 128, 0, stream>>>(part_o, part_lse, seq_lens, (__half*)out,
+                                                       Hq, D, max_parts, Tpart, cap);
+  else
+    lse_merge_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(
+        part_o, part_lse, seq_lens, (__nv_bfloat16*)out, Hq, D, max_parts, Tpart, cap);
+  return cudaGetLastError();
+}
+
+}  // namespace llmc
