@@ -55,6 +55,7 @@ struct Params {
   const int32_t* seq_lens;
   int32_t* status;
   int B, Hq, Hkv, G, HG, P, max_pages, T, max_parts, num_pages, nstages;
+  int max_entries;   // block-table entries one work item can touch (T / P + 2)
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -65,11 +66,13 @@ __device__ __forceinline__ uint32_t swz(int row, int chunk) {
 }
 
 struct Item {
-  int b, part, kvh, hg, t0, t1;
+  int b, part, kvh, hg, t0, t1, L;
 };
 
+// Work item i -> (sequence, partition, KV head, head group).  Reads only shared
+// memory: the item prefix sums and the (clamped) sequence lengths.
 __device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int Hkv, int HG,
-                                            const int32_t* seq_lens, int T, int cap) {
+                                            const int* lens, int T) {
   // prefix[b] = number of items before sequence b; binary search for b.
   int lo = 0, hi = B;  // prefix[lo] <= i < prefix[hi]
   while (hi - lo > 1) {
@@ -84,9 +87,9 @@ __device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int
   const int kh = r - it.part * per_part;
   it.kvh = kh / HG;
   it.hg = kh - it.kvh * HG;
-  const int L = min(seq_lens[it.b], cap);
+  it.L = lens[it.b];
   it.t0 = it.part * T;
-  it.t1 = min(L, it.t0 + T);
+  it.t1 = min(it.L, it.t0 + T);
   return it;
 }
 
@@ -99,6 +102,14 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   constexpr int HALF_BYTES = kStageTok * kRowBytes;          // 8 KB
   constexpr int KV_BYTES = HALVES * HALF_BYTES;              // K (or V) of one stage
   constexpr int STAGE_BYTES = 2 * KV_BYTES;
+  // d = 128: one 3-D TMA box {64 cols, 2 halves, rows} brings a whole (page, head)
+  // chunk, landing as [token][half][64] (swizzle row = 2*token + half).  Other head
+  // dims use one 2-D box per 64-column half, landing as [half][token][64].
+  constexpr bool kInterleave = (D == 128);
+  auto smem_off = [](int tok, int d0) -> uint32_t {
+    return kInterleave ? swz(tok * 2 + (d0 >> 6), (d0 & 63) >> 3)
+                       : (d0 >> 6) * HALF_BYTES + swz(tok, (d0 & 63) >> 3);
+  };
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -111,7 +122,9 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(comb_l + kConsumers * 8);
   uint64_t* empty_bar = full_bar + kMaxStages;
   int* prefix = reinterpret_cast<int*>(empty_bar + kMaxStages);       // [B + 1]
-  volatile int* abort_flag = prefix + p.B + 1;
+  int* lens = prefix + p.B + 1;                                        // [B]
+  int* bt_s = lens + p.B;                                              // [2][max_entries]
+  volatile int* abort_flag = bt_s + 2 * p.max_entries;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -152,7 +165,8 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int run = incl - sum;
     for (int b = lo; b < hi; ++b) {
       prefix[b] = run;
-      int L = min(p.seq_lens[b], p.max_pages * p.P);
+      const int L = min(p.seq_lens[b], p.max_pages * p.P);
+      lens[b] = L;
       run += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
     }
     if (lane == 31) prefix[p.B] = incl;
@@ -162,10 +176,37 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
 
   if (warp == kConsumers) {
     // ======================= producer warp =======================
+    // The block-table slice of the NEXT item is prefetched with cp.async into the
+    // other half of a double buffer while the current item's stages are issued,
+    // so no stage waits on a dependent global load.
     uint32_t stage = 0;
-    for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
-      const Item it = decode_item(i, prefix, p.B, p.Hkv, p.HG, p.seq_lens, p.T, p.max_pages * p.P);
-      const int32_t* bt = p.block_table + (size_t)it.b * p.max_pages;
+    auto prefetch_bt = [&](const Item& it, int buf) {
+      const int32_t* row = p.block_table + (size_t)it.b * p.max_pages;
+      const int first = it.t0 / p.P;
+      const int n = (it.t1 - 1) / p.P - first + 1;
+      const uint32_t dst = smem_u32(bt_s + buf * p.max_entries);
+      for (int e = lane; e < n; e += 32) cp_async_4(dst + 4 * e, row + first + e);
+      cp_async_commit();
+    };
+    int buf = 0;
+    Item it{};
+    if ((int)blockIdx.x < total_items) {
+      it = decode_item(blockIdx.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
+      prefetch_bt(it, 0);
+    }
+    for (int i = blockIdx.x; i < total_items; i += gridDim.x, buf ^= 1) {
+      Item nx{};
+      const bool has_next = i + (int)gridDim.x < total_items;
+      if (has_next) {
+        nx = decode_item(i + gridDim.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
+        prefetch_bt(nx, buf ^ 1);
+        cp_async_wait<1>();      // this item's slice has landed (the next may be in flight)
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncwarp();
+      const int* ids = bt_s + buf * p.max_entries;
+      const int item_first = it.t0 / p.P;
       const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
       for (int s = 0; s < nstage; ++s, ++stage) {
         const int slot = stage % nst;
@@ -179,33 +220,41 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
           first_page = tok0 / p.P; row0 = 0; rows = p.P;
           npg = min(kStageTok / p.P, (it.t1 - first_page * p.P + p.P - 1) / p.P);
         }
-        // Lane j < npg fetches page id j of this stage.
+        // Lane j < npg takes page id j of this stage.
         int page = 0;
         bool page_ok = true;
         if (lane < npg) {
-          page = bt[first_page + lane];
+          page = ids[first_page - item_first + lane];
           if (page < 0 || page >= p.num_pages) {
             atomicOr(p.status, kStatusBadPage);
             page_ok = false;
           }
         }
         const unsigned okmask = __ballot_sync(0xffffffffu, lane < npg && page_ok);
-        const int nboxes = __popc(okmask) * HALVES * 2;
-        const uint32_t bytes = nboxes * rows * kRowBytes;
+        const uint32_t bytes = __popc(okmask) * 2u * HALVES * rows * kRowBytes;  // K + V
         const uint32_t fb = smem_u32(&full_bar[slot]);
         mbar_wait_bounded(smem_u32(&empty_bar[slot]), (round & 1u) ^ 1u, abort_flag, p.status);
         if (lane == 0) mbar_arrive_expect_tx(fb, bytes);
         __syncwarp();
         if (!*abort_flag && lane < npg && page_ok) {
           const int row = (page * p.Hkv + it.kvh) * p.P + row0;
-          const uint32_t kdst = smem_u32(ring + slot * STAGE_BYTES) + lane * rows * kRowBytes;
+          const uint32_t sbase = smem_u32(ring + slot * STAGE_BYTES);
+          if constexpr (kInterleave) {
+            const uint32_t kdst = sbase + lane * rows * HALVES * kRowBytes;
+            tma_load_3d(kdst, &tmap_k, 0, 0, row, fb);
+            tma_load_3d(kdst + KV_BYTES, &tmap_v, 0, 0, row, fb);
+          } else {
+            const uint32_t kdst = sbase + lane * rows * kRowBytes;
 #pragma unroll
-          for (int h = 0; h < HALVES; ++h) {
-            tma_load_2d(kdst + h * HALF_BYTES, &tmap_k, h * 64, row, fb);
-            tma_load_2d(kdst + KV_BYTES + h * HALF_BYTES, &tmap_v, h * 64, row, fb);
+            for (int h = 0; h < HALVES; ++h) {
+              tma_load_2d(kdst + h * HALF_BYTES, &tmap_k, h * 64, row, fb);
+              tma_load_2d(kdst + KV_BYTES + h * HALF_BYTES, &tmap_v, h * 64, row, fb);
+            }
           }
         }
       }
+      __syncwarp();   // all lanes done with this buffer before it is refilled
+      it = nx;
     }
     // Drain: wait (bounded) for the last load issued into every slot.
     if (lane == 0) {
@@ -223,23 +272,37 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const int c = lane & 3;    // fragment column pair
   const T* qbase = reinterpret_cast<const T*>(p.q);
   uint32_t stage = 0;
-  for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
-    const Item it = decode_item(i, prefix, p.B, p.Hkv, p.HG, p.seq_lens, p.T, p.max_pages * p.P);
-    const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
-    const int ghead = it.hg * 8 + g;           // head within the GQA group (column n = g)
-    const bool head_ok = ghead < p.G;
-    const int hq_n = it.kvh * p.G + ghead;
-
-    // Q^T as the B operand (k = head_dim, n = head): b0b1 = q[n][16kc+2c..], b2b3 = +8.
-    uint32_t qf[KC][2];
-    {
-      const T* qrow = qbase + ((size_t)it.b * p.Hq + (head_ok ? hq_n : 0)) * D;
+  // Q^T as the B operand (k = head_dim, n = head): b0b1 = q[n][16kc+2c..], b2b3 = +8.
+  // The next item's fragments are loaded while the current item runs.
+  auto load_q = [&](const Item& it, uint32_t (&dst)[KC][2]) {
+    const int ghead = it.hg * 8 + g;
+    const bool ok = ghead < p.G;
+    const T* qrow = qbase + ((size_t)it.b * p.Hq + (ok ? it.kvh * p.G + ghead : 0)) * D;
 #pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-        qf[kc][0] = head_ok ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c) : 0u;
-        qf[kc][1] = head_ok ? *reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c + 8) : 0u;
-      }
+    for (int kc = 0; kc < KC; ++kc) {
+      dst[kc][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c)) : 0u;
+      dst[kc][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c + 8)) : 0u;
     }
+  };
+  uint32_t qf_next[KC][2];
+  Item it_next{};
+  if ((int)blockIdx.x < total_items) {
+    it_next = decode_item(blockIdx.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
+    load_q(it_next, qf_next);
+  }
+  for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
+    const Item it = it_next;
+    uint32_t qf[KC][2];
+#pragma unroll
+    for (int kc = 0; kc < KC; ++kc) {
+      qf[kc][0] = qf_next[kc][0];
+      qf[kc][1] = qf_next[kc][1];
+    }
+    if (i + (int)gridDim.x < total_items) {
+      it_next = decode_item(i + gridDim.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
+      load_q(it_next, qf_next);
+    }
+    const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
     float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
     float l_run[2] = {0.f, 0.f};               // per-thread partial sums
     float o[KC][4];                            // O^T fragments: rows d, cols heads
@@ -259,11 +322,17 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         // Rows past the context may hold stale or never-written bytes (possibly
         // NaN); probabilities there are 0 but 0*NaN is NaN, so zero V's rows.
         const int nchunk = (kStageTok - nvalid) * 8;
-#pragma unroll
-        for (int h = 0; h < HALVES; ++h)
-          for (int k = lane; k < nchunk; k += 32)
-            *reinterpret_cast<uint4*>(vst + h * HALF_BYTES + nvalid * kRowBytes + k * 16) =
+        if constexpr (kInterleave) {
+          for (int k = lane; k < nchunk * HALVES; k += 32)
+            *reinterpret_cast<uint4*>(vst + nvalid * HALVES * kRowBytes + k * 16) =
                 make_uint4(0, 0, 0, 0);
+        } else {
+#pragma unroll
+          for (int h = 0; h < HALVES; ++h)
+            for (int k = lane; k < nchunk; k += 32)
+              *reinterpret_cast<uint4*>(vst + h * HALF_BYTES + nvalid * kRowBytes + k * 16) =
+                  make_uint4(0, 0, 0, 0);
+        }
         fence_proxy_async_smem();
         __syncwarp();
       }
@@ -272,16 +341,18 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const int ntiles = (nvalid + 15) >> 4;
 
       // ---- S^T = K . Q^T for up to 4 tiles of 16 tokens ----
+      // kc outer, tiles inner: four independent accumulation chains in flight.
       float sacc[4][4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
-        if (t < ntiles) {
-          const int row = t * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+      for (int t = 0; t < 4; ++t) sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
 #pragma unroll
-          for (int kc = 0; kc < KC; ++kc) {
-            const int d0 = kc * 16 + (lane >> 4) * 8;
-            const uint32_t addr = kaddr + (d0 >> 6) * HALF_BYTES + swz(row, (d0 & 63) >> 3);
+      for (int kc = 0; kc < KC; ++kc) {
+        const int d0 = kc * 16 + (lane >> 4) * 8;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          if (t < ntiles) {
+            const int row = t * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const uint32_t addr = kaddr + smem_off(row, d0);
             uint32_t a[4];
             ldsm_x4(addr, a[0], a[1], a[2], a[3]);
             Mma<T>::run(sacc[t], a, qf[kc][0], qf[kc][1]);
@@ -337,7 +408,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #pragma unroll
           for (int mt = 0; mt < KC; ++mt) {
             const int d0 = mt * 16 + ((lane >> 3) & 1) * 8;
-            const uint32_t addr = vaddr + (d0 >> 6) * HALF_BYTES + swz(vrow, (d0 & 63) >> 3);
+            const uint32_t addr = vaddr + smem_off(vrow, d0);
             uint32_t a[4];
             ldsm_x4_trans(addr, a[0], a[1], a[2], a[3]);
             Mma<T>::run(o[mt], a, b0, b1);
@@ -372,7 +443,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     const int nh = min(8, p.G - it.hg * 8);
-    const bool single = min(p.seq_lens[it.b], p.max_pages * p.P) <= p.T;  // one partition
+    const bool single = it.L <= p.T;  // the sequence has one partition
     for (int idx = threadIdx.x; idx < nh * D; idx += kConsumers * 32) {
       const int n = idx / D;
       const int d = idx - n * D;
@@ -588,7 +659,9 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2-D view of a page pool [num_pages * Hkv * P rows, D cols], box {64 cols, rows}.
+// View of a page pool [num_pages * Hkv * P rows, D cols] for TMA.  D = 128: 3-D
+// {64 cols, 2 halves (stride 128 B), rows (stride 256 B)}, box {64, 2, rows};
+// otherwise 2-D {D cols, rows}, box {64, rows}.  128-byte swizzle either way.
 static bool encode_pool_map(CUtensorMap* map, const void* base, long long nrows, int D, int rows,
                             std::string* err) {
   EncodeTiledFn fn = get_encode_fn();
@@ -596,13 +669,24 @@ static bool encode_pool_map(CUtensorMap* map, const void* base, long long nrows,
     *err = "cuTensorMapEncodeTiled is not available from the CUDA driver";
     return false;
   }
-  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)nrows};
-  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-  cuuint32_t box[2] = {64u, (cuuint32_t)rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (D == 128) {
+    cuuint64_t dims[3] = {64u, 2u, (cuuint64_t)nrows};
+    cuuint64_t strides[2] = {128u, (cuuint64_t)D * 2};
+    cuuint32_t box[3] = {64u, 2u, (cuuint32_t)rows};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box,
+           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)nrows};
+    cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+    cuuint32_t box[2] = {64u, (cuuint32_t)rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box,
+           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) {
     *err = "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r);
     return false;
@@ -636,7 +720,7 @@ bool fast_path_applies(int dtype, int D, int P, int max_pages, int Tpart, int B,
   const bool p_ok = (P == 8 || P == 16 || P == 32 || P == 64) || (P % fast::kStageTok == 0) ||
                     max_pages == 1;
   if (!p_ok) return false;
-  if (B > 8192) return false;
+  if (B > 4096) return false;
   auto al = [](const void* x) { return (reinterpret_cast<uintptr_t>(x) & 15) == 0; };
   return al(q) && al(kp) && al(vp);
 }
@@ -652,8 +736,10 @@ static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const v
     return cudaErrorInvalidValue;
   const DeviceInfo di = device_info();
   constexpr int STAGE_BYTES = 2 * (D / 64) * fast::kStageTok * fast::kRowBytes;
+  p.max_entries = p.T / p.P + 2;
   const size_t fixed = 1024 /*align*/ + sizeof(float) * (fast::kConsumers * D * 8 + 16 * fast::kConsumers) +
-                       2 * fast::kMaxStages * sizeof(uint64_t) + sizeof(int) * (p.B + 2) + 64;
+                       2 * fast::kMaxStages * sizeof(uint64_t) +
+                       sizeof(int) * (2 * p.B + 2 + 2 * p.max_entries) + 64;
   const size_t budget = (size_t)di.max_smem_optin;
   int nst = (int)((budget - fixed) / STAGE_BYTES);
   if (nst > fast::kMaxStages) nst = fast::kMaxStages;
