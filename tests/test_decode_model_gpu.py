@@ -1,0 +1,121 @@
+"""GPU parity of the config-5 decode model (the caller of the decode path)."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from llm_cuda_b200.models.llama3.decode_model import DecodeConfig, DecodeGraph, Llama3DecodeModel
+from llm_cuda_b200.models.llama3.rotary import build_rope_cache
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda", 0)
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def test_tiny_llama_paged_decode_matches_reference():
+    """Reference's own paged-decode parity test (tests/test_llama3_shapes.py:152-198):
+    same weights and ids; the reference's logits come from its CPU model."""
+    g = np.load(os.path.join(GOLD, "tiny_llama_fp32.npz"))
+    V, H, I, Lyr, Hq, Hkv = (int(x) for x in g["cfg"])
+    cfg = DecodeConfig(vocab_size=V, hidden_size=H, intermediate_size=I, num_hidden_layers=Lyr,
+                       num_attention_heads=Hq, num_key_value_heads=Hkv)
+    sd = {k[3:]: torch.from_numpy(g[k]) for k in g.files if k.startswith("w__")}
+    m = Llama3DecodeModel.from_reference_state_dict(cfg, sd, DEV, torch.float32, max_positions=64)
+    ids = torch.from_numpy(g["ids"]).to(DEV)
+    prefill = int(g["prefill"])
+    cache = m.make_cache(1, 32, page_size=4, shuffle_seed=3)
+    last = m.prefill(ids[:, :prefill], cache)
+    np.testing.assert_allclose(last.cpu().numpy(), g["full_logits"][:, prefill - 1], rtol=1e-4,
+                               atol=1e-4)
+    steps = [m.decode_step(ids[:, i], cache) for i in range(prefill, ids.shape[1])]
+    cache.check_status()
+    got = torch.stack(steps, dim=1).cpu().numpy()
+    np.testing.assert_allclose(got, g["step_logits"], rtol=1e-4, atol=1e-4)
+
+
+def _reference_attn_core(model):
+    """The reference's decode branch on the GPU in the model dtype: torch RoPE
+    (rotary.py:104-109), plain append, get_kv gather, _repeat_kv + _torch_attention
+    (attention.py:56-89)."""
+
+    def core(li, q, k, v, lc):
+        pos = lc.length
+        d = q.shape[-1]
+        cos, sin = build_rope_cache(1, d, model.cfg.rope_theta, torch.device("cpu"), q.dtype, pos)
+        cos, sin = cos.to(q.device)[None, None], sin.to(q.device)[None, None]
+
+        def rot(x):
+            h = x.shape[-1] // 2
+            return (x * cos) + (torch.cat((-x[..., h:], x[..., :h]), -1) * sin)
+
+        q, k = rot(q), rot(k)
+        lc.append(k, v)
+        kc, vc = lc.get_kv()
+        rep = q.shape[1] // kc.shape[1]
+        kc = kc.repeat_interleave(rep, dim=1)
+        vc = vc.repeat_interleave(rep, dim=1)
+        s = torch.matmul(q, kc.transpose(-2, -1)) / (d ** 0.5)
+        return torch.matmul(torch.softmax(s, dim=-1), vc)
+
+    return core
+
+
+def test_llama8b_shape_step_matches_reference_attention():
+    """Full Llama-3-8B layer shapes (2 layers), bf16, B=8: the fused CUDA path vs the
+    reference's torch decode branch on identical weights and caches."""
+    cfg = DecodeConfig(num_hidden_layers=2)
+    m = Llama3DecodeModel.random_init(cfg, DEV, torch.bfloat16, seed=5, max_positions=512)
+    B, S = 8, 200
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(1)).to(DEV)
+    cache = m.make_cache(B, 256, page_size=16, shuffle_seed=1)
+    m.prefill(ids, cache)
+    kp = [(lc.key_pages.clone(), lc.value_pages.clone(), lc.seq_lens.clone())
+          for lc in cache.layer_caches]
+    nxt = ids[:, -1]
+    ours = m.decode_step(nxt, cache).float()
+    for lc, (k0, v0, l0) in zip(cache.layer_caches, kp):
+        lc.key_pages.copy_(k0)
+        lc.value_pages.copy_(v0)
+        lc.seq_lens.copy_(l0)
+        lc.host_lengths = [S] * B
+    m.attn_core = _reference_attn_core(m)
+    ref = m.decode_step(nxt, cache).float()
+    m.attn_core = None
+    cache.check_status()
+    err = (ours - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 2e-2 * max(1.0, scale), (err, scale)
+    agree = (ours.argmax(-1) == ref.argmax(-1)).float().mean().item()
+    assert agree >= 0.75, agree
+
+
+def test_decode_graph_replay_matches_eager():
+    cfg = DecodeConfig(vocab_size=1000, hidden_size=512, intermediate_size=1024,
+                       num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2)
+    m = Llama3DecodeModel.random_init(cfg, DEV, torch.bfloat16, seed=9, max_positions=256)
+    B, S, steps = 4, 40, 5
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(2)).to(DEV)
+
+    def run(graph: bool):
+        cache = m.make_cache(B, 64, page_size=16, shuffle_seed=4)
+        logits = m.prefill(ids, cache)
+        nxt = logits.argmax(-1)
+        out = []
+        if graph:
+            gr = DecodeGraph(m, cache, nxt, partition_tokens=64)
+            for _ in range(steps):
+                gr.replay()
+                out.append(gr.next_ids.clone())
+        else:
+            for _ in range(steps):
+                nxt = m.decode_step(nxt, cache, partition_tokens=64).argmax(-1)
+                out.append(nxt.clone())
+        torch.cuda.synchronize()
+        cache.check_status()
+        assert cache.get_layer(0).host_lengths == [S + steps] * B
+        assert cache.get_layer(1).seq_lens.tolist() == [S + steps] * B
+        return torch.stack(out)
+
+    assert torch.equal(run(True), run(False))
