@@ -10,7 +10,7 @@ reference's column split of q/k/v_proj) — strong scaling, no data-path
 collective.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3|c4]
+                    [--workload c2|c3|c4|c5] [--compare-triton]
 
 ``--impl reference`` times the reference's CPU path (the oracle restatement in
 ``oracle/``) on the host cores with the same metric; under torchrun only rank 0
@@ -254,6 +254,57 @@ def _max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def triton_reference_compare(sets, lengths) -> dict:
+    """Time the reference's own GPU kernel, ``triton_decode_attention``
+    (``src/llm_cuda/kernels/triton/decode_attention.py:204-287`` of llm-cuda,
+    installed unmodified in ``baseline/_ref``), on this step's data.  It needs dense
+    ``[B, Hkv, L, d]`` K/V, so the pages are gathered first (the reference's
+    ``get_kv``, ``kv_cache.py:65-83``, does the same copy each step); the gather is
+    timed separately."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "llm_cuda")):
+        return {"unavailable": "baseline/_ref not installed"}
+    if len(set(lengths)) != 1:
+        return {"unavailable": "ragged batch: the reference kernel takes one kv_len"}
+    sys.path.insert(0, ref)
+    from llm_cuda.kernels.triton.decode_attention import triton_decode_attention as ref_decode
+
+    st = sets[0]
+    c = st["cache"]
+    L = lengths[0]
+    n = math.ceil(L / c.page_size)
+    idx = c.block_table[:, :n].long()
+
+    def gather(pages):
+        g = pages[idx].permute(0, 2, 1, 3, 4).reshape(c.batch_size, c.num_kv_heads,
+                                                      n * c.page_size, c.head_dim)
+        return g[:, :, :L].contiguous()
+
+    q = st["q_rot"]
+    k, v = gather(c.key_pages), gather(c.value_pages)
+    out_ref = ref_decode(q, k, v)
+    torch.cuda.synchronize()
+    times = {}
+    for name, fn in (("gather_ms", lambda: (gather(c.key_pages), gather(c.value_pages))),
+                     ("kernel_ms", lambda: ref_decode(q, k, v))):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times[name] = e0.elapsed_time(e1) / 20
+    kv = sum(lengths) * c.num_kv_heads * c.head_dim * 4
+    ours = st["out"].float()
+    return {"kernel": "llm_cuda triton_decode_attention (baseline/_ref, Triton JIT for sm_100)",
+            "kernel_ms": times["kernel_ms"], "gather_ms": times["gather_ms"],
+            "kv_gbs_kernel_only": kv / (times["kernel_ms"] * 1e-3) / 1e9,
+            "kv_gbs_with_gather": kv / ((times["kernel_ms"] + times["gather_ms"]) * 1e-3) / 1e9,
+            "max_abs_diff_vs_ours": (out_ref[:, :, 0].float() - ours).abs().max().item()}
+
+
 def run_ours(args, name, w, lengths):
     from llm_cuda_b200 import _native as N
     from llm_cuda_b200.kernels.decode_attention import choose_partition_tokens, paged_decode
@@ -339,11 +390,13 @@ def run_ours(args, name, w, lengths):
         e1 = torch.cuda.Event(enable_timing=True)
         _barrier(world)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_steps")
         with torch.cuda.stream(stream):
             e0.record(stream)
             for i in range(args.steps):
                 graphs[i % n_sets].replay()
             e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         _barrier(world)
         ms = e0.elapsed_time(e1) / args.steps
@@ -359,6 +412,7 @@ def run_ours(args, name, w, lengths):
     clocks = clock.summary()
     for st in sets:
         st["cache"].check_status()
+    tri = triton_reference_compare(sets, lengths) if args.compare_triton else None
     ms = _max_over_ranks(ms, world)
     k_ms = _max_over_ranks(k_ms, world)
 
@@ -428,6 +482,124 @@ def run_ours(args, name, w, lengths):
             "gpu_launches": 3 * args.steps,
             "clocks": clocks,
         }
+        if tri is not None:
+            line["reference_gpu_kernel"] = tri
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_c5(args):
+    """Config 5: full decode step of a random-init Llama-3-8B-shaped model, B=64, paged KV
+    prefilled to 2048 tokens (page 16), head-sharded TP over the ranks with NCCL
+    all-reduce after o_proj and down_proj; K timed greedy decode steps, each replayed
+    from one CUDA graph of the whole step."""
+    from llm_cuda_b200 import _native as N
+    from llm_cuda_b200.kernels.decode_attention import choose_partition_tokens
+    from llm_cuda_b200.models.llama3.decode_model import (
+        DecodeConfig, DecodeGraph, Llama3DecodeModel, TensorParallel)
+
+    N.load()
+    world, rank, local = _dist_setup(args)
+    dev = torch.device("cuda", local if world > 1 else 0)
+    cfg = DecodeConfig()
+    B, prompt, P = 64, 2048, 16
+    steps = args.steps
+    cap = prompt + steps + 16
+    model = Llama3DecodeModel.random_init(cfg, dev, torch.bfloat16, seed=1005,
+                                          tp=TensorParallel(rank, world), max_positions=cap)
+    cache = model.make_cache(B, cap, page_size=P, shuffle_seed=1005 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, prompt),
+                        generator=torch.Generator().manual_seed(1005)).to(dev)
+    with torch.no_grad():
+        first = model.prefill(ids, cache).argmax(-1)
+    torch.cuda.synchronize()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    T = choose_partition_tokens([prompt + steps] * B, model.hkv, model.hq // model.hkv, sms,
+                                cap)
+    graph = DecodeGraph(model, cache, first, partition_tokens=T)
+    lens0 = cache.get_layer(0).seq_lens.clone()
+
+    def reset():
+        for lc in cache.layer_caches:
+            lc.seq_lens.copy_(lens0)
+            lc.host_lengths = [prompt] * B
+        graph.ids.copy_(first)
+
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+        if cache.get_layer(0).host_lengths[0] >= prompt + steps:
+            reset()
+    reset()
+    torch.cuda.synchronize()
+    cache.check_status()
+    w_bytes, _ = model.bytes_per_step(cache)
+    kv_total = sum((prompt + i + 1) * B * model.hkv * cfg.head_dim * 2 * 2 * cfg.num_hidden_layers
+                   for i in range(steps))
+    _barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    clock = ClockSampler(dev.index if world > 1 else 0)
+    with clock:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_steps")
+        e0.record(stream)
+        for _ in range(steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+        _barrier(world)
+    cache.check_status()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    # e2e: host ids in (pinned), greedy ids out, eager public API per step
+    reset()
+    h_ids = torch.empty(B, dtype=torch.long, pin_memory=True)
+    h_ids.copy_(first.cpu())
+    h_out = torch.empty(B, dtype=torch.long, pin_memory=True)
+    e2e_steps = min(steps, 16)
+    _barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        for _ in range(e2e_steps):
+            d_ids = h_ids.to(dev, non_blocking=True)
+            nxt = model.decode_step(d_ids, cache, partition_tokens=T).argmax(-1)
+            h_out.copy_(nxt, non_blocking=True)
+            torch.cuda.synchronize()
+            h_ids.copy_(h_out)
+    e2e_ms = _max_over_ranks((time.perf_counter() - t0) / e2e_steps * 1e3, world)
+    clocks = clock.summary()
+    peaks = _peaks()
+    bytes_rank = w_bytes + kv_total / steps                 # per rank per step
+    if rank == 0:
+        line = {
+            "metric": "decode tokens/s (config 5 full decode step)", "value": B / (ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init N(0,0.02) weights, random prompt ids)",
+            "hbm_gbs_per_gpu": bytes_rank / (ms * 1e-3) / 1e9,
+            "hbm_frac_per_gpu": bytes_rank / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "config": {"workload": "config5 Llama-3-8B-shaped decode: 32 layers, hidden 4096, "
+                                   "Hq32 Hkv8 d128, ffn 14336, vocab 128256, B64, KV prefilled "
+                                   "to 2048 (page 16), greedy decode",
+                       "parallelism": f"tp{world} (head-sharded, NCCL all-reduce after "
+                                      "o_proj/down_proj)",
+                       "partition_tokens": T, "graph": "whole step (32 layers + lm_head + "
+                                                       "argmax) replayed from one CUDA graph",
+                       "weight_bytes_per_rank": w_bytes,
+                       "kv_bytes_per_rank_per_step_avg": kv_total / steps},
+            "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
+                    "path": "Llama3DecodeModel.decode_step eager + argmax, host ids in/out"},
+            "gpu_launches": 3 * cfg.num_hidden_layers * steps,
+            "clocks": clocks,
+        }
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
@@ -441,10 +613,19 @@ def main():
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["c5"], default="c2")
+    ap.add_argument("--compare-triton", action="store_true",
+                    help="also time the reference's Triton decode kernel (baseline/_ref)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of oracle CPU-baseline sampling at N=1 (0: skip)")
     args = ap.parse_args()
+    if args.workload == "c5":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 5 reference arm not "
+                              "run: the CPU model at Llama-3-8B size takes minutes per step"}))
+            return
+        run_c5(args)
+        return
     w = WORKLOADS[args.workload]
     lengths = _lengths(args.workload, w)
     if args.impl == "reference":

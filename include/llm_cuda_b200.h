@@ -105,8 +105,9 @@ LLMC_API int llmc_num_partitions(int max_tokens, int partition_tokens);
  *   q   [B, Hq, d]; out [B, Hq, d] (same dtype)
  *   k_pages, v_pages [num_pages, Hkv, page_size, d]
  *   block_table [B, max_pages_per_seq] int32; seq_lens [B] int32 (tokens to attend)
- *   partition_tokens: split-K partition length (multiple of 64).  Sequences with more
- *     than one partition leave normalised partials + log2-sum-exp in part_o/part_lse
+ *   partition_tokens: split-K bound T (multiple of 64).  A context of L tokens is cut
+ *     into n = ceil(L / T) partitions of equal length (L / n rounded up to 64).
+ *     Sequences with n > 1 leave normalised partials + log2-sum-exp in part_o/part_lse
  *     for llmc_lse_merge; single-partition sequences are written to out directly.
  *   part_o/part_lse: see llmc_decode_partials_bytes with
  *     max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);

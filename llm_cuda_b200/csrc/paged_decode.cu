@@ -29,6 +29,14 @@
 
 namespace llmc {
 
+// A context of L tokens is split into n = ceil(L / T) partitions of equal length
+// (rounded up to a multiple of 64, never above T), so that the work items of one
+// sequence are the same size.  Every partition is non-empty: (n-1)*len <= (n-1)*T < L.
+__host__ __device__ __forceinline__ int part_len(int L, int T) {
+  const int n = (L + T - 1) / T;
+  return n > 0 ? ((((L + n - 1) / n) + 63) & ~63) : T;
+}
+
 // ---------------------------------------------------------------------------
 // Fast kernel
 // ---------------------------------------------------------------------------
@@ -88,8 +96,9 @@ __device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int
   it.kvh = kh / HG;
   it.hg = kh - it.kvh * HG;
   it.L = lens[it.b];
-  it.t0 = it.part * T;
-  it.t1 = min(it.L, it.t0 + T);
+  const int plen = part_len(it.L, T);
+  it.t0 = it.part * plen;
+  it.t1 = min(it.L, it.t0 + plen);
   return it;
 }
 
@@ -497,10 +506,11 @@ paged_decode_simt_kernel(const T* __restrict__ q, const T* __restrict__ k_pages,
     if (threadIdx.x == 0 && part == 0 && kvh == 0) atomicOr(status, kStatusSeqLenRange);
     L = max_pages * P;
   }
-  const int t0 = part * Tpart;
-  if (t0 >= L) return;
-  const int t1 = min(L, t0 + Tpart);
   const int nparts = (L + Tpart - 1) / Tpart;
+  if (part >= nparts) return;
+  const int plen = part_len(L, Tpart);
+  const int t0 = part * plen;
+  const int t1 = min(L, t0 + plen);
 
   float* qs = sm;                    // [G][D]
   float* acc = qs + G * D;           // [G][D]

@@ -46,6 +46,13 @@ def _num_sms(device: torch.device) -> int:
     return _sm_count[idx]
 
 
+def part_len(L: int, T: int) -> int:
+    """Tokens per partition when a context of ``L`` is split at ``partition_tokens = T``:
+    ``n = ceil(L / T)`` equal parts rounded up to 64 (mirrors ``part_len`` in the kernels)."""
+    n = -(-L // T)
+    return ((-(-L // n) + 63) // 64) * 64 if n > 0 else T
+
+
 def choose_partition_tokens(lengths, num_kv_heads: int, heads_per_kv: int, num_sms: int,
                             max_tokens: int | None = None) -> int:
     """Split-K partition length for the persistent kernel.
@@ -70,8 +77,9 @@ def choose_partition_tokens(lengths, num_kv_heads: int, heads_per_kv: int, num_s
         # item sizes in kernel order
         sizes = []
         for L, n in zip(lens.tolist(), nparts.tolist()):
-            tok = np.full(n, T, dtype=np.int64)
-            tok[-1] = L - (n - 1) * T
+            plen = part_len(L, T)
+            tok = np.full(n, plen, dtype=np.int64)
+            tok[-1] = L - (n - 1) * plen
             sizes.append(np.repeat(tok, per_part))
         sizes = np.concatenate(sizes) + _ITEM_OVERHEAD_TOKENS
         load = np.bincount(np.arange(sizes.size) % num_sms, weights=sizes, minlength=num_sms)
