@@ -136,6 +136,28 @@ LLMC_API int llmc_lse_merge(const float* part_o, const float* part_lse, const in
                    int B, int Hq, int d, int max_parts, int partition_tokens, int dtype,
                    llmc_stream_t stream);
 
+/*
+ * Paged decode attention (decode + LSE merge, as llmc_paged_decode followed by
+ * llmc_lse_merge) for callers that cannot allocate device memory, e.g. a host
+ * framework that owns all GPU memory and gives a plugin only its input and output
+ * buffers.  No counterpart in the reference.  The split-K workspace is a fixed
+ * 8 MiB array inside the library (held on every GPU that loads it until exit);
+ * calls needing more than llmc_paged_decode_noalloc_capacity_bytes() of partials
+ * (B * Hq * max_parts * (d + 1) * 4 bytes) return LLMC_EINVAL.  The first call on a
+ * device looks up the array's address; make it before any stream capture.  All calls
+ * share the array, so calls that overlap on the GPU race: issue them in order on one
+ * stream.  Arguments as llmc_paged_decode, minus part_o/part_lse/flags.
+ */
+LLMC_API int llmc_paged_decode_noalloc(const void* q, const void* k_pages, const void* v_pages,
+                                       const int32_t* block_table, const int32_t* seq_lens,
+                                       void* out, int32_t* status, int B, int Hq, int Hkv, int d,
+                                       int page_size, int max_pages_per_seq, int num_pages,
+                                       int partition_tokens, float scale, int dtype,
+                                       llmc_stream_t stream);
+
+/* Bytes of the built-in scratch of llmc_paged_decode_noalloc (no counterpart in the reference). */
+LLMC_API size_t llmc_paged_decode_noalloc_capacity_bytes(void);
+
 /* Message of the last failed call on this host thread ("" if none). */
 LLMC_API const char* llmc_last_error_string(void);
 

@@ -36,6 +36,8 @@ SIGNATURES = {
     "llmc_num_partitions": (_I, [_I, _I]),
     "llmc_paged_decode": (_I, [_P] * 9 + [_I] * 8 + [_F, _I, _I, _P]),
     "llmc_lse_merge": (_I, [_P, _P, _P, _P] + [_I] * 6 + [_P]),
+    "llmc_paged_decode_noalloc": (_I, [_P] * 7 + [_I] * 8 + [_F, _I, _P]),
+    "llmc_paged_decode_noalloc_capacity_bytes": (_SZ, []),
     "llmc_last_error_string": (ctypes.c_char_p, []),
     "llmc_version": (ctypes.c_char_p, []),
 }

@@ -40,6 +40,11 @@ int cuda_fail(cudaError_t e, const char* where, const std::string& extra = "") {
 bool valid_dtype(int dt) { return dt == LLMC_F32 || dt == LLMC_F16 || dt == LLMC_BF16; }
 }  // namespace
 
+namespace llmc {
+// Lets other translation units of the library report through llmc_last_error_string.
+void set_last_error(const std::string& msg) { g_last_error = msg; }
+}  // namespace llmc
+
 extern "C" {
 
 const char* llmc_last_error_string(void) { return g_last_error.c_str(); }
