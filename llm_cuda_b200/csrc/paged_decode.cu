@@ -43,13 +43,17 @@ __host__ __device__ __forceinline__ int part_len(int L, int T) {
 namespace fast {
 
 constexpr int kStageTok = 64;          // tokens per pipeline stage
-// Consumer warps.  Stage st lives in ring slot st % nstages and is consumed by
-// warp st % kConsumers; nstages is a multiple of kConsumers, so every slot is
-// always consumed by the same warp.  That keeps each mbarrier wait at most one
-// phase behind the barrier, which parity waits require: were two warps to share
-// a slot, a warp could wait on a phase parity that an earlier round already
-// completed and run ahead on stale data.
-constexpr int kConsumers = 3;
+// Consumer warps, in kGroups groups of kWarpsPerGroup.  Stage st lives in ring
+// slot st % nstages and is consumed by group st % kGroups; nstages is a multiple
+// of kGroups, so every slot is always consumed by the same group.  That keeps
+// each mbarrier wait at most one phase behind the barrier, which parity waits
+// require: were two groups to share a slot, a warp could wait on a phase parity
+// that an earlier round already completed and run ahead on stale data.  Within a
+// group each warp takes its own 16-token tiles of the stage and keeps its own
+// softmax state; the item epilogue merges all consumer warps.
+constexpr int kGroups = 3;
+constexpr int kWarpsPerGroup = 2;
+constexpr int kConsumers = kGroups * kWarpsPerGroup;
 constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr int kMaxStages = 12;
 constexpr int kRowBytes = 128;         // one swizzle row = 64 bf16/fp16 elements
@@ -102,13 +106,13 @@ __device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int
   return it;
 }
 
-template <int D, typename T>
+template <int D, typename T, int ST>
 __global__ void __launch_bounds__(kThreads, 1)
 paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const Params p) {
   constexpr int HALVES = D / 64;
   constexpr int KC = D / 16;                    // k-chunks of 16 along head_dim
-  constexpr int HALF_BYTES = kStageTok * kRowBytes;          // 8 KB
+  constexpr int HALF_BYTES = ST * kRowBytes;          // 8 KB
   constexpr int KV_BYTES = HALVES * HALF_BYTES;              // K (or V) of one stage
   constexpr int STAGE_BYTES = 2 * KV_BYTES;
   // d = 128: one 3-D TMA box {64 cols, 2 halves, rows} brings a whole (page, head)
@@ -134,6 +138,8 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   int* lens = prefix + p.B + 1;                                        // [B]
   int* bt_s = lens + p.B;                                              // [2][max_entries]
   volatile int* abort_flag = bt_s + 2 * p.max_entries;
+  int* comb_count = bt_s + 2 * p.max_entries + 1;        // warps done with the current item
+  volatile int* comb_done = bt_s + 2 * p.max_entries + 2; // items combined so far
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -142,9 +148,11 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   if (threadIdx.x == 0) {
     for (int s = 0; s < nst; ++s) {
       mbar_init(smem_u32(&full_bar[s]), 1);
-      mbar_init(smem_u32(&empty_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), kWarpsPerGroup);
     }
     *abort_flag = 0;
+    *comb_count = 0;
+    *comb_done = 0;
     fence_mbarrier_init();
   }
   if (warp == kConsumers) {
@@ -216,18 +224,18 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       __syncwarp();
       const int* ids = bt_s + buf * p.max_entries;
       const int item_first = it.t0 / p.P;
-      const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
+      const int nstage = (it.t1 - it.t0 + ST - 1) / ST;
       for (int s = 0; s < nstage; ++s, ++stage) {
         const int slot = stage % nst;
         const uint32_t round = stage / nst;
-        const int tok0 = it.t0 + s * kStageTok;
+        const int tok0 = it.t0 + s * ST;
         // Pages touched by this stage and the box (rows) loaded from each.
         int npg, rows, first_page, row0;
-        if (p.P >= kStageTok) {
-          npg = 1; rows = kStageTok; first_page = tok0 / p.P; row0 = tok0 - first_page * p.P;
+        if (p.P >= ST) {
+          npg = 1; rows = ST; first_page = tok0 / p.P; row0 = tok0 - first_page * p.P;
         } else {
           first_page = tok0 / p.P; row0 = 0; rows = p.P;
-          npg = min(kStageTok / p.P, (it.t1 - first_page * p.P + p.P - 1) / p.P);
+          npg = min(ST / p.P, (it.t1 - first_page * p.P + p.P - 1) / p.P);
         }
         // Lane j < npg takes page id j of this stage.
         int page = 0;
@@ -299,6 +307,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     it_next = decode_item(blockIdx.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
     load_q(it_next, qf_next);
   }
+  int item_seq = 0;   // items this CTA has finished
   for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
     const Item it = it_next;
     uint32_t qf[KC][2];
@@ -311,116 +320,129 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       it_next = decode_item(i + gridDim.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
       load_q(it_next, qf_next);
     }
-    const int nstage = (it.t1 - it.t0 + kStageTok - 1) / kStageTok;
+    const int nstage = (it.t1 - it.t0 + ST - 1) / ST;
     float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
     float l_run[2] = {0.f, 0.f};               // per-thread partial sums
     float o[KC][4];                            // O^T fragments: rows d, cols heads
 #pragma unroll
     for (int mt = 0; mt < KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
+    constexpr int NT = ST / 16;                 // 16-token tiles per stage
+    constexpr int NTL = NT / kWarpsPerGroup;    // tiles of this warp
+    const int sub = warp % kWarpsPerGroup;
     for (int s = 0; s < nstage; ++s, ++stage) {
-      if ((int)(stage % kConsumers) != warp) continue;
+      if ((int)(stage % kGroups) != warp / kWarpsPerGroup) continue;
       const int slot = stage % nst;
       const uint32_t round = stage / nst;
       mbar_wait_bounded(smem_u32(&full_bar[slot]), round & 1u, abort_flag, p.status);
-      const int tok0 = it.t0 + s * kStageTok;
-      const int nvalid = min(kStageTok, it.t1 - tok0);
+      const int tok0 = it.t0 + s * ST;
+      const int nvalid = min(ST, it.t1 - tok0);
+      const int row_lo = sub * NTL * 16;               // this warp's token rows
+      const int my_valid = min(max(nvalid - row_lo, 0), NTL * 16);
+      const int my_tiles = (my_valid + 15) >> 4;
       uint8_t* kst = ring + slot * STAGE_BYTES;
       uint8_t* vst = kst + KV_BYTES;
-      if (nvalid < kStageTok) {
-        // Rows past the context may hold stale or never-written bytes (possibly
-        // NaN); probabilities there are 0 but 0*NaN is NaN, so zero V's rows.
-        const int nchunk = (kStageTok - nvalid) * 8;
-        if constexpr (kInterleave) {
-          for (int k = lane; k < nchunk * HALVES; k += 32)
-            *reinterpret_cast<uint4*>(vst + nvalid * HALVES * kRowBytes + k * 16) =
-                make_uint4(0, 0, 0, 0);
-        } else {
-#pragma unroll
-          for (int h = 0; h < HALVES; ++h)
-            for (int k = lane; k < nchunk; k += 32)
-              *reinterpret_cast<uint4*>(vst + h * HALF_BYTES + nvalid * kRowBytes + k * 16) =
+      if (my_tiles > 0) {
+        if (my_valid < my_tiles * 16) {
+          // Rows past the context may hold stale or never-written bytes (possibly
+          // NaN); probabilities there are 0 but 0*NaN is NaN, so zero the V rows
+          // of this warp's last tile beyond the context.
+          const int r0 = row_lo + my_valid, r1 = row_lo + my_tiles * 16;
+          const int nchunk = (r1 - r0) * 8;
+          if constexpr (kInterleave) {
+            for (int k = lane; k < nchunk * HALVES; k += 32)
+              *reinterpret_cast<uint4*>(vst + r0 * HALVES * kRowBytes + k * 16) =
                   make_uint4(0, 0, 0, 0);
+          } else {
+#pragma unroll
+            for (int h = 0; h < HALVES; ++h)
+              for (int k = lane; k < nchunk; k += 32)
+                *reinterpret_cast<uint4*>(vst + h * HALF_BYTES + r0 * kRowBytes + k * 16) =
+                    make_uint4(0, 0, 0, 0);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
         }
-        fence_proxy_async_smem();
-        __syncwarp();
-      }
-      const uint32_t kaddr = smem_u32(kst);
-      const uint32_t vaddr = smem_u32(vst);
-      const int ntiles = (nvalid + 15) >> 4;
+        const uint32_t kaddr = smem_u32(kst);
+        const uint32_t vaddr = smem_u32(vst);
 
-      // ---- S^T = K . Q^T for up to 4 tiles of 16 tokens ----
-      // kc outer, tiles inner: four independent accumulation chains in flight.
-      float sacc[4][4];
+        // ---- S^T = K . Q^T for this warp's tiles (kc outer: independent chains) ----
+        // Two accumulators per tile (even / odd k-chunks) halve the dependent mma chain.
+        float sacc[NTL][4], sacc2[NTL][4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) sacc[t][0] = sacc[t][1] = sacc[t][2] = sacc[t][3] = 0.f;
+        for (int j = 0; j < NTL; ++j)
 #pragma unroll
-      for (int kc = 0; kc < KC; ++kc) {
-        const int d0 = kc * 16 + (lane >> 4) * 8;
+          for (int r = 0; r < 4; ++r) sacc[j][r] = sacc2[j][r] = 0.f;
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          if (t < ntiles) {
-            const int row = t * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-            const uint32_t addr = kaddr + smem_off(row, d0);
-            uint32_t a[4];
-            ldsm_x4(addr, a[0], a[1], a[2], a[3]);
-            Mma<T>::run(sacc[t], a, qf[kc][0], qf[kc][1]);
+        for (int kc = 0; kc < KC; ++kc) {
+          const int d0 = kc * 16 + (lane >> 4) * 8;
+#pragma unroll
+          for (int j = 0; j < NTL; ++j) {
+            if (j < my_tiles) {
+              const int row = row_lo + j * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+              uint32_t a[4];
+              ldsm_x4(kaddr + smem_off(row, d0), a[0], a[1], a[2], a[3]);
+              Mma<T>::run((kc & 1) ? sacc2[j] : sacc[j], a, qf[kc][0], qf[kc][1]);
+            }
           }
         }
-      }
-      // ---- online softmax (log2 domain); c0/c2 -> head 2c, c1/c3 -> head 2c+1 ----
-      float mloc[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+        for (int j = 0; j < NTL; ++j)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const int tok = t * 16 + g + ((r >> 1) << 3);
-          const float v = (tok < nvalid) ? sacc[t][r] * p.scale_log2 : -INFINITY;
-          sacc[t][r] = v;
-          mloc[r & 1] = fmaxf(mloc[r & 1], v);
-        }
-      }
+          for (int r = 0; r < 4; ++r) sacc[j][r] += sacc2[j][r];
+        // ---- online softmax (log2 domain); c0/c2 -> head 2c, c1/c3 -> head 2c+1 ----
+        float mloc[2] = {-INFINITY, -INFINITY};
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 4));
-        mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 8));
-        mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 16));
-      }
-      float alpha[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const float mn = fmaxf(m_run[j], mloc[j]);
-        alpha[j] = exp2f(m_run[j] - mn);   // m_run = -inf -> 0
-        m_run[j] = mn;
-        l_run[j] *= alpha[j];
-      }
-#pragma unroll
-      for (int mt = 0; mt < KC; ++mt) {
-        o[mt][0] *= alpha[0]; o[mt][1] *= alpha[1];
-        o[mt][2] *= alpha[0]; o[mt][3] *= alpha[1];
-      }
-      // ---- P, then O^T += V^T . P^T ----
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        if (t < ntiles) {
-          float pr[4];
+        for (int j = 0; j < NTL; ++j) {
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
-            pr[r] = exp2f(sacc[t][r] - m_run[r & 1]);
-            l_run[r & 1] += pr[r];
+            const int tok = j * 16 + g + ((r >> 1) << 3);
+            const float v = (tok < my_valid) ? sacc[j][r] * p.scale_log2 : -INFINITY;
+            sacc[j][r] = v;
+            mloc[r & 1] = fmaxf(mloc[r & 1], v);
           }
-          // S^T fragment rows are tokens, columns heads; the B operand needs
-          // (k = token, n = head): transpose each 8x8 block in registers.
-          const uint32_t b0 = movmatrix_trans(Mma<T>::pack(pr[0], pr[1]));
-          const uint32_t b1 = movmatrix_trans(Mma<T>::pack(pr[2], pr[3]));
-          const int vrow = t * 16 + (lane & 7) + (lane >> 4) * 8;
+        }
 #pragma unroll
-          for (int mt = 0; mt < KC; ++mt) {
-            const int d0 = mt * 16 + ((lane >> 3) & 1) * 8;
-            const uint32_t addr = vaddr + smem_off(vrow, d0);
-            uint32_t a[4];
-            ldsm_x4_trans(addr, a[0], a[1], a[2], a[3]);
-            Mma<T>::run(o[mt], a, b0, b1);
+        for (int j = 0; j < 2; ++j) {
+          mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 4));
+          mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 8));
+          mloc[j] = fmaxf(mloc[j], __shfl_xor_sync(0xffffffffu, mloc[j], 16));
+        }
+        float alpha[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const float mn = fmaxf(m_run[j], mloc[j]);   // finite: >= 1 valid token here
+          alpha[j] = exp2f(m_run[j] - mn);               // m_run = -inf -> 0
+          m_run[j] = mn;
+          l_run[j] *= alpha[j];
+        }
+#pragma unroll
+        for (int mt = 0; mt < KC; ++mt) {
+          o[mt][0] *= alpha[0]; o[mt][1] *= alpha[1];
+          o[mt][2] *= alpha[0]; o[mt][3] *= alpha[1];
+        }
+        // ---- P, then O^T += V^T . P^T ----
+#pragma unroll
+        for (int j = 0; j < NTL; ++j) {
+          if (j < my_tiles) {
+            float pr[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              pr[r] = exp2f(sacc[j][r] - m_run[r & 1]);
+              l_run[r & 1] += pr[r];
+            }
+            // S^T fragment rows are tokens, columns heads; the B operand needs
+            // (k = token, n = head): transpose each 8x8 block in registers.
+            const uint32_t b0 = movmatrix_trans(Mma<T>::pack(pr[0], pr[1]));
+            const uint32_t b1 = movmatrix_trans(Mma<T>::pack(pr[2], pr[3]));
+            const int vrow = row_lo + j * 16 + (lane & 7) + (lane >> 4) * 8;
+#pragma unroll
+            for (int mt = 0; mt < KC; ++mt) {
+              const int d0 = mt * 16 + ((lane >> 3) & 1) * 8;
+              uint32_t a[4];
+              ldsm_x4_trans(vaddr + smem_off(vrow, d0), a[0], a[1], a[2], a[3]);
+              Mma<T>::run(o[mt], a, b0, b1);
+            }
           }
         }
       }
@@ -434,6 +456,20 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 8);
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 16);
+    }
+    // The last consumer warp to finish the item merges all warps' partial states;
+    // the others go straight on to the next item's stages, so the ring keeps
+    // streaming across item boundaries.  Before overwriting its slot, a warp checks
+    // (bounded wait) that the previous item has been merged; in practice that merge
+    // ended a whole item earlier.
+    if (item_seq > 0 && *comb_done < item_seq) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (*comb_done < item_seq && !*abort_flag) {
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+          *abort_flag = 1;
+          atomicOr(p.status, kStatusWaitTimeout);
+        }
+      }
     }
     float* my_o = comb_o + warp * D * 8;
 #pragma unroll
@@ -450,33 +486,53 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       comb_l[warp * 8 + 2 * c] = l_run[0];
       comb_l[warp * 8 + 2 * c + 1] = l_run[1];
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
-    const int nh = min(8, p.G - it.hg * 8);
-    const bool single = it.L <= p.T;  // the sequence has one partition
-    for (int idx = threadIdx.x; idx < nh * D; idx += kConsumers * 32) {
-      const int n = idx / D;
-      const int d = idx - n * D;
-      float M = -INFINITY;
+    __syncwarp();
+    __threadfence_block();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(comb_count, 1) == kConsumers - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      __threadfence_block();
+      const int nh = min(8, p.G - it.hg * 8);
+      const bool single = it.L <= p.T;  // the sequence has one partition
+      // Per-head weights once: lane n < 8 owns head n.  Warps without tokens have
+      // m = -inf and weight 0.
+      float wsc[kConsumers];
+      float M = -INFINITY, lsum = 0.f;
+      const int hn = lane & 7;
 #pragma unroll
-      for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, comb_m[w * 8 + n]);
-      float lsum = 0.f, acc = 0.f;
+      for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, comb_m[w * 8 + hn]);
 #pragma unroll
       for (int w = 0; w < kConsumers; ++w) {
-        const float sc = exp2f(comb_m[w * 8 + n] - M);   // warp without tokens: 0
-        lsum += comb_l[w * 8 + n] * sc;
-        acc += comb_o[(w * D + d) * 8 + n] * sc;
+        wsc[w] = exp2f(comb_m[w * 8 + hn] - M);
+        lsum += comb_l[w * 8 + hn] * wsc[w];
       }
-      const int hq = it.kvh * p.G + it.hg * 8 + n;
-      const size_t row = (size_t)it.b * p.Hq + hq;
-      if (single) {
-        reinterpret_cast<T*>(p.out)[row * D + d] = from_f32<T>(acc / fmaxf(lsum, 1e-9f));
-      } else {
-        const size_t pi = row * p.max_parts + it.part;
-        p.part_o[pi * D + d] = acc / lsum;
-        if (d == 0) p.part_lse[pi] = M + log2f(lsum);
+      const float inv = single ? 1.f / fmaxf(lsum, 1e-9f) : 1.f / lsum;
+      // Lane = (head hn, quarter of head_dim): 8 heads x 4 lanes.
+      const int dq = lane >> 3;
+      if (hn < nh) {
+        const int hq = it.kvh * p.G + it.hg * 8 + hn;
+        const size_t row = (size_t)it.b * p.Hq + hq;
+        for (int d = dq; d < D; d += 4) {
+          float acc = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumers; ++w) acc += comb_o[(w * D + d) * 8 + hn] * wsc[w];
+          if (single) {
+            reinterpret_cast<T*>(p.out)[row * D + d] = from_f32<T>(acc * inv);
+          } else {
+            p.part_o[(row * p.max_parts + it.part) * D + d] = acc * inv;
+          }
+        }
+        if (!single && dq == 0) p.part_lse[row * p.max_parts + it.part] = M + log2f(lsum);
+      }
+      __syncwarp();
+      if (lane == 0) {
+        *comb_count = 0;
+        __threadfence_block();
+        *comb_done = item_seq + 1;
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+    ++item_seq;
   }
 }
 
@@ -722,6 +778,7 @@ static DeviceInfo device_info() {
   return cache[dev];
 }
 
+
 bool fast_path_applies(int dtype, int D, int P, int max_pages, int Tpart, int B,
                        const void* q, const void* kp, const void* vp) {
   if (dtype != LLMC_BF16 && dtype != LLMC_F16) return false;
@@ -735,32 +792,32 @@ bool fast_path_applies(int dtype, int D, int P, int max_pages, int Tpart, int B,
   return al(q) && al(kp) && al(vp);
 }
 
-template <int D, typename T>
+template <int D, typename T, int ST>
 static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const void* vp,
                                  long long nrows, std::string* err, cudaStream_t stream) {
   fast::Params p = p0;
-  const int rows = p.P >= fast::kStageTok ? fast::kStageTok : p.P;
+  const int rows = p.P >= ST ? ST : p.P;
   CUtensorMap mk, mv;
   if (!encode_pool_map(&mk, kp, nrows, D, rows, err) ||
       !encode_pool_map(&mv, vp, nrows, D, rows, err))
     return cudaErrorInvalidValue;
   const DeviceInfo di = device_info();
-  constexpr int STAGE_BYTES = 2 * (D / 64) * fast::kStageTok * fast::kRowBytes;
+  constexpr int STAGE_BYTES = 2 * (D / 64) * ST * fast::kRowBytes;
   p.max_entries = p.T / p.P + 2;
   const size_t fixed = 1024 /*align*/ + sizeof(float) * (fast::kConsumers * D * 8 + 16 * fast::kConsumers) +
                        2 * fast::kMaxStages * sizeof(uint64_t) +
-                       sizeof(int) * (2 * p.B + 2 + 2 * p.max_entries) + 64;
+                       sizeof(int) * (2 * p.B + 4 + 2 * p.max_entries) + 64;
   const size_t budget = (size_t)di.max_smem_optin;
   int nst = (int)((budget - fixed) / STAGE_BYTES);
   if (nst > fast::kMaxStages) nst = fast::kMaxStages;
-  nst -= nst % fast::kConsumers;  // each slot is owned by one consumer warp
-  if (nst < fast::kConsumers) {
+  nst -= nst % fast::kGroups;  // each slot is owned by one consumer group
+  if (nst < fast::kGroups) {
     *err = "not enough shared memory for the decode pipeline";
     return cudaErrorInvalidValue;
   }
   p.nstages = nst;
   const size_t smem = fixed + (size_t)nst * STAGE_BYTES;
-  auto kern = fast::paged_decode_tma_kernel<D, T>;
+  auto kern = fast::paged_decode_tma_kernel<D, T, ST>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   long long upper = (long long)p.B * p.max_parts * p.Hkv * p.HG;
@@ -788,13 +845,13 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
     p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
     const long long nrows = (long long)num_pages * Hkv * P;
     if (dtype == LLMC_BF16) {
-      if (D == 64) return launch_fast_t<64, __nv_bfloat16>(p, kp, vp, nrows, err, stream);
-      if (D == 128) return launch_fast_t<128, __nv_bfloat16>(p, kp, vp, nrows, err, stream);
-      return launch_fast_t<256, __nv_bfloat16>(p, kp, vp, nrows, err, stream);
+      if (D == 64) return launch_fast_t<64, __nv_bfloat16, 64>(p, kp, vp, nrows, err, stream);
+      if (D == 128) return launch_fast_t<128, __nv_bfloat16, 64>(p, kp, vp, nrows, err, stream);
+      return launch_fast_t<256, __nv_bfloat16, 64>(p, kp, vp, nrows, err, stream);
     } else {
-      if (D == 64) return launch_fast_t<64, __half>(p, kp, vp, nrows, err, stream);
-      if (D == 128) return launch_fast_t<128, __half>(p, kp, vp, nrows, err, stream);
-      return launch_fast_t<256, __half>(p, kp, vp, nrows, err, stream);
+      if (D == 64) return launch_fast_t<64, __half, 64>(p, kp, vp, nrows, err, stream);
+      if (D == 128) return launch_fast_t<128, __half, 64>(p, kp, vp, nrows, err, stream);
+      return launch_fast_t<256, __half, 64>(p, kp, vp, nrows, err, stream);
     }
   }
   // generic SIMT path

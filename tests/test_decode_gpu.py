@@ -313,3 +313,4 @@ def test_decode_step_graph_capture():
     cache.check_status()
     assert torch.equal(out, eager)
     assert cache.seq_lens.tolist() == [L + 1 for L in lens]
+
