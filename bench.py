@@ -609,10 +609,16 @@ def run_c5(args):
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    # The step graph holds captured NCCL all-reduces: release it (and the cache)
+    # before the process group, whose teardown otherwise blocks on them.
+    del graph
+    torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
 
-        dist.destroy_process_group()
+        dist.barrier()
+        sys.stdout.flush()
+        os._exit(0)
 
 
 def main():
