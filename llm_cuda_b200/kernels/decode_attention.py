@@ -53,6 +53,9 @@ def part_len(L: int, T: int) -> int:
     return ((-(-L // n) + 63) // 64) * 64 if n > 0 else T
 
 
+_choice_cache: dict = {}
+
+
 def choose_partition_tokens(lengths, num_kv_heads: int, heads_per_kv: int, num_sms: int,
                             max_tokens: int | None = None) -> int:
     """Split-K partition length for the persistent kernel.
@@ -60,8 +63,13 @@ def choose_partition_tokens(lengths, num_kv_heads: int, heads_per_kv: int, num_s
     Simulates the kernel's static round-robin of work items (sequence-major, then
     partition, KV head, head group) over ``num_sms`` CTAs and returns the candidate
     with the smallest busiest-CTA load; each item costs its tokens plus a fixed
-    overhead, and every partition beyond the first adds a merge share.
+    overhead, and every partition beyond the first adds a merge share.  Results are
+    memoised per length vector (all layers of a step ask with the same lengths).
     """
+    key = (tuple(lengths), num_kv_heads, heads_per_kv, num_sms, max_tokens)
+    hit = _choice_cache.get(key)
+    if hit is not None:
+        return hit
     lens = np.asarray(lengths, dtype=np.int64)
     lens = lens[lens > 0]
     if lens.size == 0:
@@ -71,21 +79,22 @@ def choose_partition_tokens(lengths, num_kv_heads: int, heads_per_kv: int, num_s
     cap = int(max_tokens) if max_tokens else int(lens.max())
     best, best_cost = None, None
     for T in _PARTITION_CANDIDATES:
-        nparts = (lens + T - 1) // T
         if (cap + T - 1) // T > 4096:
             continue
-        # item sizes in kernel order
-        sizes = []
-        for L, n in zip(lens.tolist(), nparts.tolist()):
-            plen = part_len(L, T)
-            tok = np.full(n, plen, dtype=np.int64)
-            tok[-1] = L - (n - 1) * plen
-            sizes.append(np.repeat(tok, per_part))
-        sizes = np.concatenate(sizes) + _ITEM_OVERHEAD_TOKENS
+        nparts = (lens + T - 1) // T
+        plen = ((-(-lens // nparts)) + 63) // 64 * 64          # part_len, vectorised
+        seq_of_part = np.repeat(np.arange(lens.size), nparts)
+        first = np.concatenate([[0], np.cumsum(nparts)[:-1]])
+        idx_in_seq = np.arange(seq_of_part.size) - first[seq_of_part]
+        tok = np.minimum(plen[seq_of_part], lens[seq_of_part] - idx_in_seq * plen[seq_of_part])
+        sizes = np.repeat(tok, per_part) + _ITEM_OVERHEAD_TOKENS
         load = np.bincount(np.arange(sizes.size) % num_sms, weights=sizes, minlength=num_sms)
         cost = load.max() + (8 if nparts.max() > 1 else 0)
         if best_cost is None or cost < best_cost * 0.995:
             best, best_cost = T, cost
+    if len(_choice_cache) > 4096:
+        _choice_cache.clear()
+    _choice_cache[key] = best
     return best
 
 
@@ -178,7 +187,7 @@ def paged_decode(
     if out is None:
         out = torch.empty_like(q3)
     ws = workspace if workspace is not None else _default_workspace(q.device)
-    max_parts = lib.llmc_num_partitions(max_pages * P, partition_tokens)
+    max_parts = -(-(max_pages * P) // partition_tokens)   # llmc_num_partitions
     part_o, part_lse = ws.get(B, Hq, d, max_parts)
     st = status if status is not None else default_status(q.device)
     stream = N.stream_handle(q.device)
