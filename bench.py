@@ -353,12 +353,9 @@ def run_ours(args, name, w, lengths):
         c.seq_lens.copy_(st["base"])          # every step attends exactly the configured context
         c.host_lengths = list(base_host)
         c.append_rotary(st["q"], st["k"], st["v"], rope, q_out=st["q_rot"])
-        if ev is not None:
-            ev[0].record()
         paged_decode(st["q_rot"], c.key_pages, c.value_pages, c.block_table, c.seq_lens,
-                     partition_tokens=T, out=st["out"], workspace=c.workspace, status=c.status)
-        if ev is not None:
-            ev[1].record()
+                     partition_tokens=T, out=st["out"], workspace=c.workspace, status=c.status,
+                     events=ev)
 
     # eager warm-up (also allocates the split-K workspace before capture)
     for st in sets:

@@ -155,11 +155,14 @@ def paged_decode(
     workspace: DecodeWorkspace | None = None,
     status: torch.Tensor | None = None,
     force_generic: bool = False,
+    events=None,
 ) -> torch.Tensor:
     """Decode attention of ``q [B, Hq, d]`` (or ``[B, Hq, 1, d]``) over paged K/V.
 
     ``host_lens`` (host copy of ``seq_lens``) only steers the partition choice; the
-    kernels read the lengths on the device.  Returns ``out`` shaped like ``q``.
+    kernels read the lengths on the device.  ``events``: optional pair of CUDA events
+    recorded just before and just after the decode kernel (not the merge), for
+    timing it on its launching stream.  Returns ``out`` shaped like ``q``.
     """
     lib = N.load()
     if not q.is_cuda:
@@ -192,12 +195,16 @@ def paged_decode(
     st = status if status is not None else default_status(q.device)
     stream = N.stream_handle(q.device)
     dt = N.dtype_code(q.dtype)
+    if events is not None:
+        events[0].record()
     rc = lib.llmc_paged_decode(
         q3.data_ptr(), key_pages.data_ptr(), value_pages.data_ptr(), block_table.data_ptr(),
         seq_lens.data_ptr(), out.data_ptr(), N.ptr(part_o), N.ptr(part_lse), st.data_ptr(),
         B, Hq, Hkv, d, P, max_pages, num_pages, partition_tokens, float(scale), dt,
         N.LLMC_DECODE_FORCE_GENERIC if force_generic else 0, stream)
     N.check(rc, "llmc_paged_decode")
+    if events is not None:
+        events[1].record()
     rc = lib.llmc_lse_merge(N.ptr(part_o), N.ptr(part_lse), seq_lens.data_ptr(), out.data_ptr(),
                             B, Hq, d, max_parts, partition_tokens, dt, stream)
     N.check(rc, "llmc_lse_merge")
