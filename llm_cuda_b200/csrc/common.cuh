@@ -127,6 +127,18 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start before its predecessor finishes;
+// pdl_wait() blocks until the predecessor grid has completed and its memory is
+// visible.  pdl_launch_dependents() lets the next such kernel start its prologue.
+// Both are no-ops for kernels launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
 // cp.async (4-byte, global -> shared) for small index prefetches
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cp_async_4(uint32_t dst, const void* src) {

@@ -155,11 +155,15 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     *comb_done = 0;
     fence_mbarrier_init();
   }
+  if (warp == kConsumers && lane == 0) {
+    prefetch_tensormap(&tmap_k);
+    prefetch_tensormap(&tmap_v);
+  }
+  // Everything above overlaps the previous kernel under programmatic dependent
+  // launch; lengths, block table and pages are read only after this wait.
+  pdl_wait();
+  pdl_launch_dependents();
   if (warp == kConsumers) {
-    if (lane == 0) {
-      prefetch_tensormap(&tmap_k);
-      prefetch_tensormap(&tmap_v);
-    }
     const int per = (p.B + 31) / 32;
     const int lo = min(p.B, lane * per), hi = min(p.B, lo + per);
     const int per_part = p.Hkv * p.HG;
@@ -680,6 +684,7 @@ __global__ void __launch_bounds__(128)
 lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                  const int32_t* __restrict__ seq_lens, T* __restrict__ out, int Hq, int D,
                  int max_parts, int Tpart, int cap) {
+  pdl_wait();   // partials of the decode kernel are complete and visible
   const int h = blockIdx.x, b = blockIdx.y;
   const int L = min(seq_lens[b], cap);
   const int n = L > 0 ? (L + Tpart - 1) / Tpart : 0;
@@ -823,7 +828,18 @@ static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const v
   long long upper = (long long)p.B * p.max_parts * p.Hkv * p.HG;
   int grid = di.sms;
   if (upper < grid) grid = (int)(upper > 0 ? upper : 1);
-  kern<<<grid, fast::kThreads, smem, stream>>>(mk, mv, p);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(fast::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, mk, mv, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -885,16 +901,26 @@ cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const i
                              void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
                              int dtype, cudaStream_t stream) {
   if (B == 0 || Hq == 0) return cudaSuccess;
-  dim3 grid(Hq, B);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(Hq, B);
+  cfg.blockDim = dim3(128);
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
   if (dtype == LLMC_F32)
-    lse_merge_kernel<float><<<grid, 128, 0, stream>>>(part_o, part_lse, seq_lens, (float*)out, Hq,
-                                                      D, max_parts, Tpart, cap);
+    e = cudaLaunchKernelEx(&cfg, lse_merge_kernel<float>, part_o, part_lse, seq_lens,
+                           (float*)out, Hq, D, max_parts, Tpart, cap);
   else if (dtype == LLMC_F16)
-    lse_merge_kernel<__half><<<grid, 128, 0, stream>>>(part_o, part_lse, seq_lens, (__half*)out,
-                                                       Hq, D, max_parts, Tpart, cap);
+    e = cudaLaunchKernelEx(&cfg, lse_merge_kernel<__half>, part_o, part_lse, seq_lens,
+                           (__half*)out, Hq, D, max_parts, Tpart, cap);
   else
-    lse_merge_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(
-        part_o, part_lse, seq_lens, (__nv_bfloat16*)out, Hq, D, max_parts, Tpart, cap);
+    e = cudaLaunchKernelEx(&cfg, lse_merge_kernel<__nv_bfloat16>, part_o, part_lse, seq_lens,
+                           (__nv_bfloat16*)out, Hq, D, max_parts, Tpart, cap);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

@@ -28,7 +28,7 @@ __device__ __forceinline__ T rope_elem(T x_self, T x_partner, T c, T s, bool fir
 }
 
 template <typename T, int VEC>
-__global__ void __launch_bounds__(256) rope_append_kernel(
+__global__ void __launch_bounds__(512) rope_append_kernel(
     const T* __restrict__ q_in, const T* __restrict__ k_in, const T* __restrict__ v_in,
     T* __restrict__ q_out, T* __restrict__ k_pages, T* __restrict__ v_pages,
     const int32_t* __restrict__ block_table, int32_t* __restrict__ seq_lens,
@@ -37,6 +37,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
   using Vec = typename std::conditional<VEC * sizeof(T) == 16, uint4,
               typename std::conditional<VEC * sizeof(T) == 8, uint2, T>::type>::type;
   const int b = blockIdx.x;
+  pdl_launch_dependents();   // the decode kernel may start its prologue now
   __shared__ int s_pos0;
   __shared__ int s_ok;
   if (threadIdx.x == 0) {
@@ -135,7 +136,7 @@ static cudaError_t launch_rope_append_t(const void* q_in, const void* k_in, cons
   const bool vec_ok = (half % V16) == 0 && aligned(q_in, 16) && aligned(k_in, 16) &&
                       aligned(v_in, 16) && aligned(q_out, 16) && aligned(k_pages, 16) &&
                       aligned(v_pages, 16) && aligned(cos_tab, 16) && aligned(sin_tab, 16);
-  dim3 grid(B), block(256);
+  dim3 grid(B), block(512);
   if (vec_ok) {
     rope_append_kernel<T, V16><<<grid, block, 0, stream>>>(
         (const T*)q_in, (const T*)k_in, (const T*)v_in, (T*)q_out, (T*)k_pages, (T*)v_pages, bt,
