@@ -158,6 +158,23 @@ LLMC_API int llmc_paged_decode_noalloc(const void* q, const void* k_pages, const
 /* Bytes of the built-in scratch of llmc_paged_decode_noalloc (no counterpart in the reference). */
 LLMC_API size_t llmc_paged_decode_noalloc_capacity_bytes(void);
 
+/*
+ * Decode-step helpers around the attention path (config-5 decode loop).
+ *
+ * llmc_add_rmsnorm: x[rows, hidden] += delta (if delta != NULL), then
+ *   out = x * rsqrt(mean(x^2) + eps) * weight.  Replaces the residual add
+ *   (src/llm_cuda/models/llama3/model.py:37,42) and RMSNorm.forward's torch path
+ *   (src/llm_cuda/models/llama3/norm.py:31-33).
+ * llmc_swiglu: out[rows, inter] = silu(g) * u with gate_up[rows, 2*inter] = [g | u].
+ *   Replaces triton_swiglu's torch path (src/llm_cuda/kernels/triton/swiglu.py:103-107)
+ *   on the output of a fused gate/up projection (mlp.py:39-43).
+ * fp32 arithmetic, one rounding to the dtype per output.
+ */
+LLMC_API int llmc_add_rmsnorm(void* x, const void* delta, const void* weight, void* out, int rows,
+                              int hidden, float eps, int dtype, llmc_stream_t stream);
+LLMC_API int llmc_swiglu(const void* gate_up, void* out, int rows, int inter, int dtype,
+                         llmc_stream_t stream);
+
 /* Message of the last failed call on this host thread ("" if none). */
 LLMC_API const char* llmc_last_error_string(void);
 

@@ -21,6 +21,10 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens,
                              void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
                              int dtype, cudaStream_t stream);
+cudaError_t launch_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int rows,
+                               int hidden, float eps, int dtype, cudaStream_t stream);
+cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dtype,
+                          cudaStream_t stream);
 }  // namespace llmc
 
 namespace {
@@ -139,6 +143,31 @@ int llmc_lse_merge(const float* part_o, const float* part_lse, const int32_t* se
                                          partition_tokens, max_parts * partition_tokens, dtype,
                                          (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "llmc_lse_merge");
+  return LLMC_OK;
+}
+
+int llmc_add_rmsnorm(void* x, const void* delta, const void* weight, void* out, int rows,
+                     int hidden, float eps, int dtype, llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_add_rmsnorm: unknown dtype");
+  if (rows < 0 || hidden <= 0) return fail(LLMC_EINVAL, "llmc_add_rmsnorm: bad sizes");
+  if (!x || !weight || !out) return fail(LLMC_EINVAL, "llmc_add_rmsnorm: NULL pointer argument");
+  if (rows == 0) return LLMC_OK;
+  cudaError_t e = llmc::launch_add_rmsnorm(x, delta, weight, out, rows, hidden, eps, dtype,
+                                           (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_add_rmsnorm");
+  return LLMC_OK;
+}
+
+int llmc_swiglu(const void* gate_up, void* out, int rows, int inter, int dtype,
+                llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_swiglu: unknown dtype");
+  if (rows < 0 || inter <= 0) return fail(LLMC_EINVAL, "llmc_swiglu: bad sizes");
+  if (!gate_up || !out) return fail(LLMC_EINVAL, "llmc_swiglu: NULL pointer argument");
+  if (rows == 0) return LLMC_OK;
+  cudaError_t e = llmc::launch_swiglu(gate_up, out, rows, inter, dtype, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_swiglu");
   return LLMC_OK;
 }
 

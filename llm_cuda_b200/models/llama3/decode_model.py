@@ -31,6 +31,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
+from ...kernels.step_ops import add_rmsnorm, swiglu
 from .kv_cache import PagedKVCache, make_block_table
 from .rotary import RopeTable
 
@@ -205,9 +206,22 @@ class Llama3DecodeModel:
 
     def _mlp(self, L: dict, x: torch.Tensor) -> torch.Tensor:
         gu = F.linear(x, L["wgu"])
-        gate, up = gu.split(self.inter, dim=-1)
-        h = (gate * torch.sigmoid(gate)) * up             # swiglu.py:103-107
+        if gu.is_cuda:
+            h = swiglu(gu)                                 # fused CUDA kernel
+        else:
+            gate, up = gu.split(self.inter, dim=-1)
+            h = (gate * torch.sigmoid(gate)) * up         # swiglu.py:103-107
         return self.tp.all_reduce_(F.linear(h, L["wdown"]))
+
+    def _add_norm(self, x: torch.Tensor, w: torch.Tensor, delta: torch.Tensor | None):
+        """Residual add (model.py:37,42) + RMSNorm (norm.py:31-33): returns ``(x, h)``.
+        On CUDA one fused kernel updates ``x`` in place; the CPU branch serves only the
+        CPU-rank tests of the TP plumbing."""
+        if x.is_cuda:
+            return x, add_rmsnorm(x, w, self.cfg.rms_norm_eps, delta=delta)
+        if delta is not None:
+            x = x + delta
+        return x, rms_norm(x, w, self.cfg.rms_norm_eps)
 
     def prefill(self, ids: torch.Tensor, cache: PagedKVCache) -> torch.Tensor:
         """Process prompts ``ids [B, S]`` into an EMPTY cache; returns last-token logits.
@@ -217,10 +231,11 @@ class Llama3DecodeModel:
         """
         cfg = self.cfg
         B, S = ids.shape
-        x = F.embedding(ids, self.embed)
+        x = F.embedding(ids, self.embed).contiguous()
+        delta = None
         for li, L in enumerate(self.layers):
             lc = cache.get_layer(li)
-            h = rms_norm(x, L["in_norm"], cfg.rms_norm_eps)
+            x, h = self._add_norm(x, L["in_norm"], delta)
             q, k, v = self._split_qkv(F.linear(h, L["wqkv"]), B, S)
             q_rot = lc.append_rotary(q, k, v, self.rope)
             kc, vc = lc.get_kv()                             # rotated k as stored
@@ -229,11 +244,11 @@ class Llama3DecodeModel:
                 q_rot, kc.repeat_interleave(rep, dim=1), vc.repeat_interleave(rep, dim=1),
                 is_causal=True)
             attn = attn.transpose(1, 2).reshape(B, S, self.hq * cfg.head_dim)
-            x = x + self.tp.all_reduce_(F.linear(attn, L["wo"]))
-            h = rms_norm(x, L["post_norm"], cfg.rms_norm_eps)
-            x = x + self._mlp(L, h)
-        x = rms_norm(x[:, -1], self.final_norm, cfg.rms_norm_eps)
-        return F.linear(x, self.lm_head)
+            o = self.tp.all_reduce_(F.linear(attn, L["wo"]))
+            x, h = self._add_norm(x, L["post_norm"], o)
+            delta = self._mlp(L, h)
+        x, h = self._add_norm(x, self.final_norm, delta)
+        return F.linear(h[:, -1], self.lm_head)
 
     def decode_step(self, ids: torch.Tensor, cache: PagedKVCache,
                     partition_tokens: int | None = None) -> torch.Tensor:
@@ -241,9 +256,10 @@ class Llama3DecodeModel:
         cfg = self.cfg
         B = ids.shape[0]
         x = F.embedding(ids.view(B, 1), self.embed)          # [B, 1, H]
+        delta = None
         for li, L in enumerate(self.layers):
             lc = cache.get_layer(li)
-            h = rms_norm(x, L["in_norm"], cfg.rms_norm_eps)
+            x, h = self._add_norm(x, L["in_norm"], delta)
             q, k, v = self._split_qkv(F.linear(h, L["wqkv"]), B, 1)
             if self.attn_core is not None:
                 attn = self.attn_core(li, q, k, v, lc)
@@ -251,11 +267,11 @@ class Llama3DecodeModel:
                 q_rot = lc.append_rotary(q, k, v, self.rope)  # fused RoPE + page append
                 attn = lc.decode(q_rot, partition_tokens=partition_tokens)
             attn = attn.reshape(B, 1, self.hq * cfg.head_dim)
-            x = x + self.tp.all_reduce_(F.linear(attn, L["wo"]))
-            h = rms_norm(x, L["post_norm"], cfg.rms_norm_eps)
-            x = x + self._mlp(L, h)
-        x = rms_norm(x[:, 0], self.final_norm, cfg.rms_norm_eps)
-        return F.linear(x, self.lm_head)
+            o = self.tp.all_reduce_(F.linear(attn, L["wo"]))
+            x, h = self._add_norm(x, L["post_norm"], o)
+            delta = self._mlp(L, h)
+        x, h = self._add_norm(x, self.final_norm, delta)
+        return F.linear(h[:, 0], self.lm_head)
 
     def bytes_per_step(self, cache: PagedKVCache) -> tuple[int, int]:
         """(weight bytes, KV bytes) this rank reads in one decode step at the current
