@@ -125,6 +125,34 @@ LLMC_API int llmc_paged_decode(const void* q, const void* k_pages, const void* v
                       llmc_stream_t stream);
 
 /*
+ * One decode step of attention with RoPE and the KV-page append fused in:
+ * llmc_rope_append (S = 1) + llmc_paged_decode + llmc_lse_merge in two launches.
+ *
+ * Replaces the decode branch of Llama3Attention.forward between the projections and
+ * o_proj (src/llm_cuda/models/llama3/attention.py:110-139): build_rope_cache +
+ * apply_rotary (rotary.py:29-109), PagedKVLayerCache.append (kv_cache.py:38-63),
+ * get_kv (kv_cache.py:65-83) and triton_decode_attention (decode_attention.py:204-287).
+ *
+ *   q [B, Hq, d] raw (un-rotated) query of the new token; k_new, v_new [B, Hkv, d].
+ *   seq_lens [B]: lengths BEFORE the step; the new token goes to position seq_lens[b]
+ *     and on completion seq_lens[b] has grown by one (written by the merge launch).
+ *   q_rot_out [B, Hq, d]: receives the rotated query (required).
+ *   lens_next [B] int32 scratch.  Other arguments as llmc_rope_append / llmc_paged_decode.
+ * In the fused kernel every CTA rotates its query fragments in registers and the warp
+ * whose tile holds the new token rotates k and patches k/v into the landed tile and
+ * the page.  Shapes the fused kernel does not take run the three separate kernels.
+ */
+LLMC_API int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
+                                     void* q_rot_out, void* k_pages, void* v_pages,
+                                     const int32_t* block_table, int32_t* seq_lens,
+                                     const void* cos_tab, const void* sin_tab, int rope_max_pos,
+                                     void* out, float* part_o, float* part_lse,
+                                     int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
+                                     int d, int page_size, int max_pages_per_seq, int num_pages,
+                                     int partition_tokens, float scale, int dtype,
+                                     llmc_stream_t stream);
+
+/*
  * Log-sum-exp merge of split-K partials into out [B, Hq, d].  For each (b, h)
  * with n = ceil(seq_lens[b] / partition_tokens) partitions: n >= 2 merges, n == 1
  * leaves out untouched (already written by llmc_paged_decode), n == 0 writes

@@ -38,6 +38,7 @@ SIGNATURES = {
     "llmc_lse_merge": (_I, [_P, _P, _P, _P] + [_I] * 6 + [_P]),
     "llmc_paged_decode_noalloc": (_I, [_P] * 7 + [_I] * 8 + [_F, _I, _P]),
     "llmc_paged_decode_noalloc_capacity_bytes": (_SZ, []),
+    "llmc_rope_append_decode": (_I, [_P] * 10 + [_I] + [_P] * 5 + [_I] * 8 + [_F, _I, _P]),
     "llmc_add_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _I, _P]),
     "llmc_swiglu": (_I, [_P, _P, _I, _I, _I, _P]),
     "llmc_last_error_string": (ctypes.c_char_p, []),

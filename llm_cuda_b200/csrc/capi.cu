@@ -21,6 +21,13 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens,
                              void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
                              int dtype, cudaStream_t stream);
+cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void* v_new,
+                                void* q_rot_out, void* kp, void* vp, const int32_t* bt,
+                                int32_t* seq_lens, const void* cos_tab, const void* sin_tab,
+                                int rope_max_pos, void* out, float* part_o, float* part_lse,
+                                int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
+                                int D, int P, int max_pages, int num_pages, int Tpart,
+                                float scale, int dtype, std::string* err, cudaStream_t stream);
 cudaError_t launch_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int rows,
                                int hidden, float eps, int dtype, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dtype,
@@ -143,6 +150,57 @@ int llmc_lse_merge(const float* part_o, const float* part_lse, const int32_t* se
                                          partition_tokens, max_parts * partition_tokens, dtype,
                                          (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "llmc_lse_merge");
+  return LLMC_OK;
+}
+
+int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new, void* q_rot_out,
+                            void* k_pages, void* v_pages, const int32_t* block_table,
+                            int32_t* seq_lens, const void* cos_tab, const void* sin_tab,
+                            int rope_max_pos, void* out, float* part_o, float* part_lse,
+                            int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d,
+                            int page_size, int max_pages_per_seq, int num_pages,
+                            int partition_tokens, float scale, int dtype, llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_rope_append_decode: unknown dtype");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
+      num_pages <= 0 || partition_tokens <= 0 || rope_max_pos <= 0)
+    return fail(LLMC_EINVAL, "llmc_rope_append_decode: sizes must be positive");
+  if (Hq % Hkv) return fail(LLMC_EINVAL, "llmc_rope_append_decode: Hq must be a multiple of Hkv");
+  if (d % 2 || d > 256)
+    return fail(LLMC_EUNSUPPORTED, "llmc_rope_append_decode: head_dim must be even and <= 256");
+  if (partition_tokens % 64)
+    return fail(LLMC_EINVAL, "llmc_rope_append_decode: partition_tokens must be a multiple of 64");
+  if ((long long)Hq / Hkv * d > 16384)
+    return fail(LLMC_EUNSUPPORTED, "llmc_rope_append_decode: (Hq/Hkv) * head_dim > 16384");
+  if ((long long)num_pages * Hkv * page_size >= (1ll << 31))
+    return fail(LLMC_EUNSUPPORTED, "llmc_rope_append_decode: page pool rows exceed 2^31");
+  if (!q || !k_new || !v_new || !q_rot_out || !k_pages || !v_pages || !block_table || !seq_lens ||
+      !cos_tab || !sin_tab || !out || !lens_next || !status)
+    return fail(LLMC_EINVAL, "llmc_rope_append_decode: NULL pointer argument");
+  const int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
+  if (max_parts > 1 && (!part_o || !part_lse))
+    return fail(LLMC_EINVAL, "llmc_rope_append_decode: part_o/part_lse are required");
+  if (B == 0) return LLMC_OK;
+  std::string err;
+  cudaError_t e = llmc::launch_fused_decode(
+      q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens, cos_tab, sin_tab,
+      rope_max_pos, out, part_o, part_lse, lens_next, status, B, Hq, Hkv, d, page_size,
+      max_pages_per_seq, num_pages, partition_tokens, scale, dtype, &err, (cudaStream_t)stream);
+  if (e == cudaErrorNotSupported) {
+    // Shape outside the fused kernel: the same step with the separate kernels.
+    cudaGetLastError();
+    int rc = llmc_rope_append(q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens,
+                              cos_tab, sin_tab, B, 1, Hq, Hkv, d, page_size, max_pages_per_seq,
+                              num_pages, rope_max_pos, dtype, status, stream);
+    if (rc) return rc;
+    rc = llmc_paged_decode(q_rot_out, k_pages, v_pages, block_table, seq_lens, out, part_o,
+                           part_lse, status, B, Hq, Hkv, d, page_size, max_pages_per_seq,
+                           num_pages, partition_tokens, scale, dtype, 0, stream);
+    if (rc) return rc;
+    return llmc_lse_merge(part_o, part_lse, seq_lens, out, B, Hq, d, max_parts,
+                          partition_tokens, dtype, stream);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_rope_append_decode", err);
   return LLMC_OK;
 }
 

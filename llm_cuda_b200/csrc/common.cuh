@@ -239,4 +239,34 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16_rn(x);
 }
 
+// One RoPE output element with the reference's torch rounding (rotary.py:104-109):
+// first half  x*cos + (-x_partner)*sin, second half x*cos + x_partner*sin; each
+// product and the sum are rounded to T (no FMA contraction).
+template <typename T>
+__device__ __forceinline__ T rope_elem(T x_self, T x_partner, T c, T s, bool first_half) {
+  const float xs = to_f32(x_self);
+  const float xp = first_half ? -to_f32(x_partner) : to_f32(x_partner);
+  const T a = from_f32<T>(__fmul_rn(xs, to_f32(c)));
+  const T b = from_f32<T>(__fmul_rn(xp, to_f32(s)));
+  return from_f32<T>(__fadd_rn(to_f32(a), to_f32(b)));
+}
+
+// Rotate two packed pairs (x1 = elements i, i+1 of the first half; x2 = the same
+// elements of the second half) with packed cos/sin pairs of columns i, i+1.
+template <typename T>
+__device__ __forceinline__ void rope_pair2(uint32_t& x1, uint32_t& x2, uint32_t cs, uint32_t sn) {
+  T* a = reinterpret_cast<T*>(&x1);
+  T* b = reinterpret_cast<T*>(&x2);
+  const T* c = reinterpret_cast<const T*>(&cs);
+  const T* s = reinterpret_cast<const T*>(&sn);
+  T o1[2], o2[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    o1[e] = rope_elem<T>(a[e], b[e], c[e], s[e], true);
+    o2[e] = rope_elem<T>(b[e], a[e], c[e], s[e], false);
+  }
+  x1 = *reinterpret_cast<uint32_t*>(o1);
+  x2 = *reinterpret_cast<uint32_t*>(o2);
+}
+
 }  // namespace llmc

@@ -69,6 +69,19 @@ struct Params {
   int B, Hq, Hkv, G, HG, P, max_pages, T, max_parts, num_pages, nstages;
   int max_entries;   // block-table entries one work item can touch (T / P + 2)
   float scale_log2;  // softmax scale * log2(e)
+  // Fused RoPE + append (FUSE kernels only).  q holds the RAW query; the new token of
+  // sequence b sits at position seq_lens[b] (lengths before the append): its q and k
+  // are rotated here with cos/sin row pos, k/v are written to the pages, and the
+  // advanced lengths go to lens_next (published into seq_lens by the merge kernel).
+  const void* k_new;       // [B, Hkv, D]
+  const void* v_new;       // [B, Hkv, D]
+  const void* cos_tab;     // [rope_max_pos, D]
+  const void* sin_tab;
+  void* k_pages;           // pools written with the new token
+  void* v_pages;
+  void* q_rot_out;         // [B, Hq, D] rotated query (written once per head)
+  int32_t* lens_next;      // [B]
+  int rope_max_pos;
 };
 
 // Byte offset of (row, 16-byte chunk) inside a 128B-swizzled region whose base is
@@ -106,7 +119,7 @@ __device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int
   return it;
 }
 
-template <int D, typename T, int ST>
+template <int D, typename T, int ST, bool FUSE>
 __global__ void __launch_bounds__(kThreads, 1)
 paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
                         const __grid_constant__ CUtensorMap tmap_v, const Params p) {
@@ -168,13 +181,19 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     const int lo = min(p.B, lane * per), hi = min(p.B, lo + per);
     const int per_part = p.Hkv * p.HG;
     int sum = 0;
-    for (int b = lo; b < hi; ++b) {
-      int L = p.seq_lens[b];
+    // Tokens attended by sequence b: its length, plus the new token when fused.
+    auto eff_len = [&](int b, bool report) -> int {
+      int L = p.seq_lens[b] + (FUSE ? 1 : 0);
       const int cap = p.max_pages * p.P;
       if (L > cap) {
-        atomicOr(p.status, kStatusSeqLenRange);
+        if (report) atomicOr(p.status, FUSE ? kStatusAppendOverflow : kStatusSeqLenRange);
         L = cap;
       }
+      if (FUSE && report && L > p.rope_max_pos) atomicOr(p.status, kStatusRopeRange);
+      return L;
+    };
+    for (int b = lo; b < hi; ++b) {
+      const int L = eff_len(b, true);
       sum += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
     }
     int incl = sum;
@@ -186,8 +205,9 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     int run = incl - sum;
     for (int b = lo; b < hi; ++b) {
       prefix[b] = run;
-      const int L = min(p.seq_lens[b], p.max_pages * p.P);
+      const int L = eff_len(b, false);
       lens[b] = L;
+      if (FUSE && blockIdx.x == 0) p.lens_next[b] = L;
       run += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
     }
     if (lane == 31) prefix[p.B] = incl;
@@ -295,7 +315,11 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   uint32_t stage = 0;
   // Q^T as the B operand (k = head_dim, n = head): b0b1 = q[n][16kc+2c..], b2b3 = +8.
   // The next item's fragments are loaded while the current item runs.
-  auto load_q = [&](const Item& it, uint32_t (&dst)[KC][2]) {
+  // With FUSE the cos/sin pairs of the fragment's first-half columns at the new
+  // token's position come along; the rotation happens when the item starts.
+  constexpr int KH = KC / 2;            // k-chunks in the first half of head_dim
+  auto load_q = [&](const Item& it, uint32_t (&dst)[KC][2], uint32_t (&cs)[KH][2],
+                    uint32_t (&sn)[KH][2]) {
     const int ghead = it.hg * 8 + g;
     const bool ok = ghead < p.G;
     const T* qrow = qbase + ((size_t)it.b * p.Hq + (ok ? it.kvh * p.G + ghead : 0)) * D;
@@ -304,12 +328,25 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       dst[kc][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c)) : 0u;
       dst[kc][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c + 8)) : 0u;
     }
+    if constexpr (FUSE) {
+      const int pos = max(it.L - 1, 0);
+      const T* crow = reinterpret_cast<const T*>(p.cos_tab) + (size_t)pos * D;
+      const T* srow = reinterpret_cast<const T*>(p.sin_tab) + (size_t)pos * D;
+#pragma unroll
+      for (int kc = 0; kc < KH; ++kc)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          cs[kc][r] = __ldg(reinterpret_cast<const uint32_t*>(crow + kc * 16 + 2 * c + 8 * r));
+          sn[kc][r] = __ldg(reinterpret_cast<const uint32_t*>(srow + kc * 16 + 2 * c + 8 * r));
+        }
+    }
   };
   uint32_t qf_next[KC][2];
+  uint32_t cs_next[KH][2], sn_next[KH][2];
   Item it_next{};
   if ((int)blockIdx.x < total_items) {
     it_next = decode_item(blockIdx.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
-    load_q(it_next, qf_next);
+    load_q(it_next, qf_next, cs_next, sn_next);
   }
   int item_seq = 0;   // items this CTA has finished
   for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
@@ -320,9 +357,28 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       qf[kc][0] = qf_next[kc][0];
       qf[kc][1] = qf_next[kc][1];
     }
+    if constexpr (FUSE) {
+      // RoPE of the new token's query, in registers: element d of the first half
+      // (chunk kc) pairs with d + D/2 (chunk kc + KC/2) held by the same lane.
+#pragma unroll
+      for (int kc = 0; kc < KH; ++kc)
+#pragma unroll
+        for (int r = 0; r < 2; ++r) rope_pair2<T>(qf[kc][r], qf[kc + KH][r], cs_next[kc][r], sn_next[kc][r]);
+      // The partition-0 item of each head group publishes the rotated query.
+      const int ghead = it.hg * 8 + g;
+      if (p.q_rot_out != nullptr && it.part == 0 && warp == 0 && ghead < p.G) {
+        uint32_t* qo = reinterpret_cast<uint32_t*>(
+            reinterpret_cast<T*>(p.q_rot_out) + ((size_t)it.b * p.Hq + it.kvh * p.G + ghead) * D);
+#pragma unroll
+        for (int kc = 0; kc < KC; ++kc) {
+          qo[(kc * 16 + 2 * c) / 2] = qf[kc][0];
+          qo[(kc * 16 + 2 * c + 8) / 2] = qf[kc][1];
+        }
+      }
+    }
     if (i + (int)gridDim.x < total_items) {
       it_next = decode_item(i + gridDim.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
-      load_q(it_next, qf_next);
+      load_q(it_next, qf_next, cs_next, sn_next);
     }
     const int nstage = (it.t1 - it.t0 + ST - 1) / ST;
     float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
@@ -346,6 +402,45 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const int my_tiles = (my_valid + 15) >> 4;
       uint8_t* kst = ring + slot * STAGE_BYTES;
       uint8_t* vst = kst + KV_BYTES;
+      bool patched = false;
+      if constexpr (FUSE) {
+        // The new token lands in this warp's rows: its page slot was never written, so
+        // put the rotated k row and the v row straight into the landed tile, and into
+        // the page for later steps (one head group per KV head writes the page).
+        const int pos = it.L - 1;
+        const int r = pos - tok0;
+        if (r >= row_lo && r < row_lo + my_valid) {
+          const T* kn = reinterpret_cast<const T*>(p.k_new) + ((size_t)it.b * p.Hkv + it.kvh) * D;
+          const T* vn = reinterpret_cast<const T*>(p.v_new) + ((size_t)it.b * p.Hkv + it.kvh) * D;
+          const T* crow = reinterpret_cast<const T*>(p.cos_tab) + (size_t)pos * D;
+          const T* srow = reinterpret_cast<const T*>(p.sin_tab) + (size_t)pos * D;
+          const int page = p.block_table[(size_t)it.b * p.max_pages + pos / p.P];
+          const bool write_page = it.hg == 0 && page >= 0 && page < p.num_pages;
+          T* kp = reinterpret_cast<T*>(p.k_pages) +
+                  (((size_t)(write_page ? page : 0) * p.Hkv + it.kvh) * p.P + pos % p.P) * D;
+          T* vp = reinterpret_cast<T*>(p.v_pages) + (kp - reinterpret_cast<T*>(p.k_pages));
+          for (int i = 2 * lane; i < D / 2; i += 64) {
+            uint32_t x1 = *reinterpret_cast<const uint32_t*>(kn + i);
+            uint32_t x2 = *reinterpret_cast<const uint32_t*>(kn + i + D / 2);
+            rope_pair2<T>(x1, x2, *reinterpret_cast<const uint32_t*>(crow + i),
+                          *reinterpret_cast<const uint32_t*>(srow + i));
+            const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vn + i);
+            const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vn + i + D / 2);
+            *reinterpret_cast<uint32_t*>(kst + smem_off(r, i) + (i & 7) * 2) = x1;
+            *reinterpret_cast<uint32_t*>(kst + smem_off(r, i + D / 2) + (i & 7) * 2) = x2;
+            *reinterpret_cast<uint32_t*>(vst + smem_off(r, i) + (i & 7) * 2) = v1;
+            *reinterpret_cast<uint32_t*>(vst + smem_off(r, i + D / 2) + (i & 7) * 2) = v2;
+            if (write_page) {
+              *reinterpret_cast<uint32_t*>(kp + i) = x1;
+              *reinterpret_cast<uint32_t*>(kp + i + D / 2) = x2;
+              *reinterpret_cast<uint32_t*>(vp + i) = v1;
+              *reinterpret_cast<uint32_t*>(vp + i + D / 2) = v2;
+            }
+          }
+          patched = true;
+          __syncwarp();
+        }
+      }
       if (my_tiles > 0) {
         if (my_valid < my_tiles * 16) {
           // Rows past the context may hold stale or never-written bytes (possibly
@@ -451,6 +546,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
       }
       __syncwarp();
+      if (FUSE && patched) fence_proxy_async_smem();   // generic writes before the next TMA
       if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
     }
 
@@ -683,10 +779,14 @@ template <typename T>
 __global__ void __launch_bounds__(128)
 lse_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                  const int32_t* __restrict__ seq_lens, T* __restrict__ out, int Hq, int D,
-                 int max_parts, int Tpart, int cap) {
+                 int max_parts, int Tpart, int cap, const int32_t* __restrict__ lens_next,
+                 int32_t* __restrict__ seq_lens_out) {
   pdl_wait();   // partials of the decode kernel are complete and visible
   const int h = blockIdx.x, b = blockIdx.y;
-  const int L = min(seq_lens[b], cap);
+  // After a fused RoPE+append+decode the attended lengths are in lens_next; they
+  // become the cache's lengths here, once the decode kernel is done reading them.
+  const int L = lens_next ? lens_next[b] : min(seq_lens[b], cap);
+  if (lens_next && h == 0 && threadIdx.x == 0) seq_lens_out[b] = L;
   const int n = L > 0 ? (L + Tpart - 1) / Tpart : 0;
   const size_t row = (size_t)b * Hq + h;
   if (n == 1) return;  // written directly by the decode kernel
@@ -797,7 +897,7 @@ bool fast_path_applies(int dtype, int D, int P, int max_pages, int Tpart, int B,
   return al(q) && al(kp) && al(vp);
 }
 
-template <int D, typename T, int ST>
+template <int D, typename T, int ST, bool FUSE>
 static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const void* vp,
                                  long long nrows, std::string* err, cudaStream_t stream) {
   fast::Params p = p0;
@@ -822,7 +922,7 @@ static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const v
   }
   p.nstages = nst;
   const size_t smem = fixed + (size_t)nst * STAGE_BYTES;
-  auto kern = fast::paged_decode_tma_kernel<D, T, ST>;
+  auto kern = fast::paged_decode_tma_kernel<D, T, ST, FUSE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   long long upper = (long long)p.B * p.max_parts * p.Hkv * p.HG;
@@ -843,6 +943,56 @@ static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const v
   return cudaGetLastError();
 }
 
+static cudaError_t launch_lse_merge_ex(const float* part_o, const float* part_lse,
+                                       const int32_t* seq_lens, void* out, int B, int Hq, int D,
+                                       int max_parts, int Tpart, int cap, int dtype,
+                                       cudaStream_t stream, const int32_t* lens_next,
+                                       int32_t* seq_lens_out);
+
+template <bool FUSE>
+static cudaError_t launch_fast(const fast::Params& p, int dtype, int D, const void* kp,
+                               const void* vp, std::string* err, cudaStream_t stream) {
+  const long long nrows = (long long)p.num_pages * p.Hkv * p.P;
+  if (dtype == LLMC_BF16) {
+    if (D == 64) return launch_fast_t<64, __nv_bfloat16, 64, FUSE>(p, kp, vp, nrows, err, stream);
+    if (D == 128) return launch_fast_t<128, __nv_bfloat16, 64, FUSE>(p, kp, vp, nrows, err, stream);
+    return launch_fast_t<256, __nv_bfloat16, 64, FUSE>(p, kp, vp, nrows, err, stream);
+  }
+  if (D == 64) return launch_fast_t<64, __half, 64, FUSE>(p, kp, vp, nrows, err, stream);
+  if (D == 128) return launch_fast_t<128, __half, 64, FUSE>(p, kp, vp, nrows, err, stream);
+  return launch_fast_t<256, __half, 64, FUSE>(p, kp, vp, nrows, err, stream);
+}
+
+// Fused RoPE + page append + decode + merge (one decode launch, one merge launch).
+// Returns cudaErrorNotSupported when the fast kernel does not apply to this shape;
+// the caller then runs the separate kernels.
+cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void* v_new,
+                                void* q_rot_out, void* kp, void* vp, const int32_t* bt,
+                                int32_t* seq_lens, const void* cos_tab, const void* sin_tab,
+                                int rope_max_pos, void* out, float* part_o, float* part_lse,
+                                int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
+                                int D, int P, int max_pages, int num_pages, int Tpart,
+                                float scale, int dtype, std::string* err, cudaStream_t stream) {
+  if (B == 0) return cudaSuccess;
+  if (!fast_path_applies(dtype, D, P, max_pages, Tpart, B, q_raw, kp, vp))
+    return cudaErrorNotSupported;
+  const int G = Hq / Hkv;
+  const int max_parts = (max_pages * P + Tpart - 1) / Tpart;
+  fast::Params p;
+  p.q = q_raw; p.out = out; p.part_o = part_o; p.part_lse = part_lse; p.block_table = bt;
+  p.seq_lens = seq_lens; p.status = status;
+  p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
+  p.max_pages = max_pages; p.T = Tpart; p.max_parts = max_parts; p.num_pages = num_pages;
+  p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
+  p.k_new = k_new; p.v_new = v_new; p.cos_tab = cos_tab; p.sin_tab = sin_tab;
+  p.k_pages = kp; p.v_pages = vp; p.q_rot_out = q_rot_out; p.lens_next = lens_next;
+  p.rope_max_pos = rope_max_pos;
+  cudaError_t e = launch_fast<true>(p, dtype, D, kp, vp, err, stream);
+  if (e != cudaSuccess) return e;
+  return launch_lse_merge_ex(part_o, part_lse, seq_lens, out, B, Hq, D, max_parts, Tpart,
+                             max_parts * Tpart, dtype, stream, lens_next, seq_lens);
+}
+
 cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, const int32_t* bt,
                                 const int32_t* seq_lens, void* out, float* part_o,
                                 float* part_lse, int32_t* status, int B, int Hq, int Hkv, int D,
@@ -859,16 +1009,11 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
     p.max_pages = max_pages; p.T = Tpart; p.max_parts = max_parts; p.num_pages = num_pages;
     p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
-    const long long nrows = (long long)num_pages * Hkv * P;
-    if (dtype == LLMC_BF16) {
-      if (D == 64) return launch_fast_t<64, __nv_bfloat16, 64>(p, kp, vp, nrows, err, stream);
-      if (D == 128) return launch_fast_t<128, __nv_bfloat16, 64>(p, kp, vp, nrows, err, stream);
-      return launch_fast_t<256, __nv_bfloat16, 64>(p, kp, vp, nrows, err, stream);
-    } else {
-      if (D == 64) return launch_fast_t<64, __half, 64>(p, kp, vp, nrows, err, stream);
-      if (D == 128) return launch_fast_t<128, __half, 64>(p, kp, vp, nrows, err, stream);
-      return launch_fast_t<256, __half, 64>(p, kp, vp, nrows, err, stream);
-    }
+    p.k_new = p.v_new = p.cos_tab = p.sin_tab = nullptr;
+    p.k_pages = p.v_pages = p.q_rot_out = nullptr;
+    p.lens_next = nullptr;
+    p.rope_max_pos = 0;
+    return launch_fast<false>(p, dtype, D, kp, vp, err, stream);
   }
   // generic SIMT path
   const size_t smem = generic::smem_bytes(G, D);
@@ -897,9 +1042,24 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
   return cudaGetLastError();
 }
 
+static cudaError_t launch_lse_merge_ex(const float* part_o, const float* part_lse,
+                                       const int32_t* seq_lens, void* out, int B, int Hq, int D,
+                                       int max_parts, int Tpart, int cap, int dtype,
+                                       cudaStream_t stream, const int32_t* lens_next,
+                                       int32_t* seq_lens_out);
+
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens,
                              void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
                              int dtype, cudaStream_t stream) {
+  return launch_lse_merge_ex(part_o, part_lse, seq_lens, out, B, Hq, D, max_parts, Tpart, cap,
+                             dtype, stream, nullptr, nullptr);
+}
+
+static cudaError_t launch_lse_merge_ex(const float* part_o, const float* part_lse,
+                                       const int32_t* seq_lens, void* out, int B, int Hq, int D,
+                                       int max_parts, int Tpart, int cap, int dtype,
+                                       cudaStream_t stream, const int32_t* lens_next,
+                                       int32_t* seq_lens_out) {
   if (B == 0 || Hq == 0) return cudaSuccess;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -913,13 +1073,14 @@ cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const i
   cudaError_t e;
   if (dtype == LLMC_F32)
     e = cudaLaunchKernelEx(&cfg, lse_merge_kernel<float>, part_o, part_lse, seq_lens,
-                           (float*)out, Hq, D, max_parts, Tpart, cap);
+                           (float*)out, Hq, D, max_parts, Tpart, cap, lens_next, seq_lens_out);
   else if (dtype == LLMC_F16)
     e = cudaLaunchKernelEx(&cfg, lse_merge_kernel<__half>, part_o, part_lse, seq_lens,
-                           (__half*)out, Hq, D, max_parts, Tpart, cap);
+                           (__half*)out, Hq, D, max_parts, Tpart, cap, lens_next, seq_lens_out);
   else
     e = cudaLaunchKernelEx(&cfg, lse_merge_kernel<__nv_bfloat16>, part_o, part_lse, seq_lens,
-                           (__nv_bfloat16*)out, Hq, D, max_parts, Tpart, cap);
+                           (__nv_bfloat16*)out, Hq, D, max_parts, Tpart, cap, lens_next,
+                           seq_lens_out);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -17,16 +17,6 @@
 
 namespace llmc {
 
-template <typename T>
-__device__ __forceinline__ T rope_elem(T x_self, T x_partner, T c, T s, bool first_half) {
-  // first half:  x*cos + (-x2)*sin ; second half: x*cos + x1*sin
-  const float xs = to_f32(x_self);
-  const float xp = first_half ? -to_f32(x_partner) : to_f32(x_partner);
-  const T a = from_f32<T>(__fmul_rn(xs, to_f32(c)));
-  const T b = from_f32<T>(__fmul_rn(xp, to_f32(s)));
-  return from_f32<T>(__fadd_rn(to_f32(a), to_f32(b)));
-}
-
 template <typename T, int VEC>
 __global__ void __launch_bounds__(512) rope_append_kernel(
     const T* __restrict__ q_in, const T* __restrict__ k_in, const T* __restrict__ v_in,

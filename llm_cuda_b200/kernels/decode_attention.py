@@ -110,6 +110,12 @@ class DecodeWorkspace:
         self.part_o = torch.empty(0, dtype=torch.float32, device=device)
         self.part_lse = torch.empty(0, dtype=torch.float32, device=device)
 
+    def lens_next(self, B: int) -> torch.Tensor:
+        """int32 [B] scratch for the fused step's advanced lengths."""
+        if getattr(self, "_lens_next", None) is None or self._lens_next.numel() < B:
+            self._lens_next = torch.empty(B, dtype=torch.int32, device=self.device)
+        return self._lens_next
+
     def get(self, B: int, Hq: int, d: int, max_parts: int):
         if max_parts <= 1:
             return None, None
@@ -208,6 +214,71 @@ def paged_decode(
     rc = lib.llmc_lse_merge(N.ptr(part_o), N.ptr(part_lse), seq_lens.data_ptr(), out.data_ptr(),
                             B, Hq, d, max_parts, partition_tokens, dt, stream)
     N.check(rc, "llmc_lse_merge")
+    return out.view(q_shape)
+
+
+def rope_append_decode(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    key_pages: torch.Tensor,
+    value_pages: torch.Tensor,
+    block_table: torch.Tensor,
+    seq_lens: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    *,
+    host_lens=None,
+    partition_tokens: int | None = None,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    q_out: torch.Tensor | None = None,
+    workspace: DecodeWorkspace | None = None,
+    status: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """One fused decode-attention step (``llmc_rope_append_decode``).
+
+    ``q [B, Hq, 1, d]`` raw query, ``k``/``v`` ``[B, Hkv, 1, d]`` of the new token at
+    position ``seq_lens[b]``: RoPE, the page append and the attention over
+    ``seq_lens[b] + 1`` tokens run in one decode launch plus the merge launch, which
+    also advances ``seq_lens``.  ``host_lens`` are the lengths BEFORE the step.
+    Returns ``out`` shaped like ``q``; the rotated query goes to ``q_out``.
+    """
+    lib = N.load()
+    if not q.is_cuda:
+        raise ValueError("rope_append_decode needs CUDA tensors")
+    q_shape = q.shape
+    B, Hq, d = q.shape[0], q.shape[1], q.shape[-1]
+    if q.dim() == 4 and q.shape[2] != 1:
+        raise ValueError("one new token per sequence")
+    num_pages, Hkv, P, d_p = key_pages.shape
+    if d_p != d or k.shape[0] != B or k.shape[1] != Hkv or v.shape != k.shape:
+        raise ValueError("q/k/v shapes do not match the cache layout")
+    if key_pages.dtype != q.dtype or k.dtype != q.dtype or cos.dtype != q.dtype:
+        raise ValueError("q, k, v, pages and the RoPE table must share a dtype")
+    q = q.contiguous()
+    k = k.contiguous()
+    v = v.contiguous()
+    max_pages = block_table.shape[1]
+    if partition_tokens is None:
+        lens = [x + 1 for x in host_lens] if host_lens is not None else [max_pages * P] * B
+        partition_tokens = choose_partition_tokens(lens, Hkv, Hq // Hkv, _num_sms(q.device),
+                                                   max_tokens=max_pages * P)
+    if scale is None:
+        scale = 1.0 / math.sqrt(d)
+    out = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device) if out is None else out
+    q_out = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device) if q_out is None else q_out
+    ws = workspace if workspace is not None else _default_workspace(q.device)
+    max_parts = -(-(max_pages * P) // partition_tokens)
+    part_o, part_lse = ws.get(B, Hq, d, max_parts)
+    st = status if status is not None else default_status(q.device)
+    rc = lib.llmc_rope_append_decode(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), q_out.data_ptr(), key_pages.data_ptr(),
+        value_pages.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(), cos.data_ptr(),
+        sin.data_ptr(), cos.shape[0], out.data_ptr(), N.ptr(part_o), N.ptr(part_lse),
+        ws.lens_next(B).data_ptr(), st.data_ptr(), B, Hq, Hkv, d, P, max_pages, num_pages,
+        partition_tokens, float(scale), N.dtype_code(q.dtype), N.stream_handle(q.device))
+    N.check(rc, "llmc_rope_append_decode")
     return out.view(q_shape)
 
 

@@ -31,7 +31,11 @@ import math
 import torch
 
 from ... import _native as N
-from ...kernels.decode_attention import DecodeWorkspace, paged_decode_attention
+from ...kernels.decode_attention import (
+    DecodeWorkspace,
+    paged_decode_attention,
+    rope_append_decode,
+)
 from ...kernels.rope import rope_append
 from .rotary import RopeTable
 
@@ -149,6 +153,23 @@ class PagedKVLayerCache:
                             self.seq_lens, self.status, cos=rope.cos, sin=rope.sin, q_out=q_out)
         self.host_lengths = [x + seq for x in self.host_lengths]
         return q_rot
+
+    def rope_append_decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                           rope: RopeTable, out: torch.Tensor | None = None,
+                           q_out: torch.Tensor | None = None,
+                           partition_tokens: int | None = None) -> torch.Tensor:
+        """The whole decode-attention step of the new token: RoPE on q/k, page append
+        and paged attention over the grown context, fused into one decode kernel (plus
+        the merge).  Same results as ``append_rotary`` followed by ``decode``."""
+        seq = self._check_kv(k, v)
+        if seq != 1:
+            raise ValueError("rope_append_decode takes one new token per sequence")
+        res = rope_append_decode(q, k, v, self.key_pages, self.value_pages, self.block_table,
+                                 self.seq_lens, rope.cos, rope.sin, host_lens=self.host_lengths,
+                                 partition_tokens=partition_tokens, out=out, q_out=q_out,
+                                 workspace=self.workspace, status=self.status)
+        self.host_lengths = [x + 1 for x in self.host_lengths]
+        return res
 
     def advance_host_lengths(self, n: int) -> None:
         """Mirror ``n`` appends replayed from a CUDA graph (the device already advanced)."""

@@ -314,3 +314,101 @@ def test_decode_step_graph_capture():
     assert torch.equal(out, eager)
     assert cache.seq_lens.tolist() == [L + 1 for L in lens]
 
+
+
+# ---------------------------------------------------------------------------
+# Fused RoPE + append + decode (llmc_rope_append_decode)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("T", [None, 64])
+@pytest.mark.parametrize("name", list(C.STEP_CASES))
+def test_fused_step_matches_reference(name, T):
+    dt, Hq, Hkv, d, lens, scale, seed = C.STEP_CASES[name]
+    dtype = C.DTYPES[dt]
+    seqs = C.step_inputs(name)
+    P, B = 16, len(lens)
+    max_len = max(lens) + 16
+    max_pages = math.ceil(max_len / P)
+    gen = torch.Generator().manual_seed(seed)
+    num_pages = B * max_pages + 5
+    bt = make_block_table(B, max_pages, num_pages, max_pages, generator=gen)
+    cache = PagedKVLayerCache(Hkv, d, max_len, P, DEV, dtype, batch_size=B, num_pages=num_pages,
+                              block_table=bt)
+    poison(cache)
+    fill_pages(cache, [s[0] for s in seqs], [s[1] for s in seqs])
+    rope = RopeTable(max_len, d, C.THETA, DEV, dtype)
+    q = torch.stack([s[2] for s in seqs])[:, :, None].to(DEV)
+    k = torch.stack([s[3] for s in seqs])[:, :, None].to(DEV)
+    v = torch.stack([s[4] for s in seqs])[:, :, None].to(DEV)
+    q_rot = torch.empty(B, Hq, d, device=DEV, dtype=dtype)
+    out = cache.rope_append_decode(q, k, v, rope, q_out=q_rot, partition_tokens=T)
+    cache.check_status()
+    assert cache.seq_lens.tolist() == lens and cache.host_lengths == lens
+    g = _gold(f"step_{name}.npz")
+    np.testing.assert_array_equal(C.to_np(q_rot), g["q_rot"])
+    for b, L in enumerate(lens):
+        page = int(cache.block_table[b, (L - 1) // 16])
+        np.testing.assert_array_equal(C.to_np(cache.key_pages[page, :, (L - 1) % 16]), g["k_rot"][b])
+    assert_parity(out[:, :, 0], O.from_bits(g["out"], dt), dtype, f"fused/{name}")
+
+
+def test_fused_step_equals_separate_kernels_config2():
+    """Config 2 at full size: the fused step and append_rotary + decode give identical
+    outputs, pages and lengths (the same rounding and the same reduction order)."""
+    cache, _ = _random_paged(64, 32, 8, 128, [4096] * 64, 16, torch.bfloat16, 2010)
+    lens0 = torch.full((64,), 4095, dtype=torch.int32, device=DEV)
+    cache.seq_lens.copy_(lens0)
+    cache.host_lengths = [4095] * 64
+    rope = RopeTable(4096, 128, C.THETA, DEV, torch.bfloat16)
+    gd = torch.Generator(device=DEV).manual_seed(3)
+    q = torch.randn(64, 32, 1, 128, device=DEV, generator=gd).bfloat16()
+    k = torch.randn(64, 8, 1, 128, device=DEV, generator=gd).bfloat16()
+    v = torch.randn(64, 8, 1, 128, device=DEV, generator=gd).bfloat16()
+    kp0, vp0 = cache.key_pages.clone(), cache.value_pages.clone()
+    fused = cache.rope_append_decode(q, k, v, rope).clone()
+    kp1, vp1, l1 = cache.key_pages.clone(), cache.value_pages.clone(), cache.seq_lens.clone()
+    cache.key_pages.copy_(kp0)
+    cache.value_pages.copy_(vp0)
+    cache.seq_lens.copy_(lens0)
+    cache.host_lengths = [4095] * 64
+    sep = cache.decode(cache.append_rotary(q, k, v, rope))
+    cache.check_status()
+    assert torch.equal(cache.seq_lens, l1) and l1.tolist() == [4096] * 64
+    assert torch.equal(cache.key_pages, kp1) and torch.equal(cache.value_pages, vp1)
+    assert torch.equal(fused, sep)
+
+
+def test_fused_step_graph_replay():
+    B, Hq, Hkv, d, P = 8, 32, 8, 128, 16
+    lens = [300 + 37 * i for i in range(B)]
+    cache, _ = _random_paged(B, Hq, Hkv, d, [L + 8 for L in lens], P, torch.bfloat16, 2011)
+    rope = RopeTable(cache.max_seq_len, d, C.THETA, DEV, torch.bfloat16)
+    gd = torch.Generator(device=DEV).manual_seed(8)
+    q = torch.randn(B, Hq, 1, d, device=DEV, generator=gd).bfloat16()
+    k = torch.randn(B, Hkv, 1, d, device=DEV, generator=gd).bfloat16()
+    v = torch.randn(B, Hkv, 1, d, device=DEV, generator=gd).bfloat16()
+    out = torch.empty(B, Hq, d, device=DEV, dtype=torch.bfloat16)
+    kp0, vp0 = cache.key_pages.clone(), cache.value_pages.clone()
+
+    def reset():
+        cache.key_pages.copy_(kp0)
+        cache.value_pages.copy_(vp0)
+        cache.seq_lens.copy_(torch.tensor(lens, dtype=torch.int32))
+        cache.host_lengths = list(lens)
+
+    reset()
+    eager = cache.rope_append_decode(q, k, v, rope, partition_tokens=128).clone()
+    reset()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            cache.rope_append_decode(q, k, v, rope, out=out, partition_tokens=128)
+    torch.cuda.current_stream().wait_stream(s)
+    reset()
+    graph.replay()
+    torch.cuda.synchronize()
+    cache.check_status()
+    assert torch.equal(out.view_as(eager), eager)
+    assert cache.seq_lens.tolist() == [L + 1 for L in lens]
