@@ -310,7 +310,8 @@ def triton_reference_compare(sets, lengths) -> dict:
 
 def run_ours(args, name, w, lengths):
     from llm_cuda_b200 import _native as N
-    from llm_cuda_b200.kernels.decode_attention import choose_partition_tokens, paged_decode
+    from llm_cuda_b200.kernels.decode_attention import (
+        choose_partition_tokens, paged_decode, rope_append_decode)
     from llm_cuda_b200.models.llama3 import PagedKVLayerCache, RopeTable, make_block_table
 
     N.load()
@@ -349,13 +350,15 @@ def run_ours(args, name, w, lengths):
     base_host = [L - 1 for L in lengths]
 
     def step(st, ev=None):
+        # One fused launch does RoPE on the new token, the page append and the paged
+        # attention; the merge launch combines split-K partials and advances seq_lens.
         c = st["cache"]
         c.seq_lens.copy_(st["base"])          # every step attends exactly the configured context
         c.host_lengths = list(base_host)
-        c.append_rotary(st["q"], st["k"], st["v"], rope, q_out=st["q_rot"])
-        paged_decode(st["q_rot"], c.key_pages, c.value_pages, c.block_table, c.seq_lens,
-                     partition_tokens=T, out=st["out"], workspace=c.workspace, status=c.status,
-                     events=ev)
+        rope_append_decode(st["q"], st["k"], st["v"], c.key_pages, c.value_pages,
+                           c.block_table, c.seq_lens, rope.cos, rope.sin, host_lens=base_host,
+                           partition_tokens=T, out=st["out"], q_out=st["q_rot"],
+                           workspace=c.workspace, status=c.status, events=ev)
 
     # eager warm-up (also allocates the split-K workspace before capture)
     for st in sets:
@@ -406,6 +409,9 @@ def run_ours(args, name, w, lengths):
                for _ in range(kreps)]
         with torch.cuda.stream(stream):
             for i in range(kreps):
+                # A short device sleep ahead of each step keeps the GPU busy while the
+                # host issues the bracketed launches, so the events time device work only.
+                torch.cuda._sleep(200_000)
                 step(sets[i % n_sets], evs[i])
         torch.cuda.synchronize()
         k_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
@@ -469,9 +475,8 @@ def run_ours(args, name, w, lengths):
             vd = d_in[j][nq + nk:].view(B, hkv, 1, d)
             c.seq_lens.copy_(st["base"])
             c.host_lengths = list(base_host)
-            q_rot = c.append_rotary(qd, kd, vd, rope)
+            c.rope_append_decode(qd, kd, vd, rope, out=d_out[j].view(B, hq, 1, d))
             in_free[j].record(main_s)
-            c.decode(q_rot, out=d_out[j].view(B, hq, 1, d))
             out_ready[j].record(main_s)
     torch.cuda.synchronize()
     e2e_ms = (time.perf_counter() - t0) / e2e_steps * 1e3
@@ -481,8 +486,12 @@ def run_ours(args, name, w, lengths):
     total_kv = sum(lengths) * Hkv * d * 2 * 2         # all ranks together
     value = total_kv / (ms * 1e-3) / 1e9
     tokens_s = B / (ms * 1e-3)
-    # algorithmic bytes of one decode-kernel launch on one rank
-    alg = kv_bytes_rank + 2 * B * hq * d * 2 + sum(pages_per) * 4 + B * 4
+    # algorithmic bytes of the fused decode launch + its merge launch on one rank: K/V
+    # of the whole context, raw q in, rotated q and out written, the new token's k/v
+    # read and appended, block table, split-K partials written and read back
+    parts = sum(math.ceil(L / T) for L in lengths) if max(lengths) > T else 0
+    alg = (kv_bytes_rank + 3 * B * hq * d * 2 + 2 * 2 * B * hkv * d * 2 + sum(pages_per) * 4
+           + B * 4 + 2 * parts * hq * (d + 1) * 4)
     achieved = alg / (k_ms * 1e-3) / 1e9
     peaks = _peaks()
     if rank == 0:
@@ -504,7 +513,7 @@ def run_ours(args, name, w, lengths):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "traffic": _profile_traffic(name, world),
-                         "kernel": "paged_decode_tma_kernel<128,bf16>",
+                         "kernel": "paged_decode_tma_kernel<128,bf16,64,fused> + lse_merge_kernel",
                          "kernel_ms": k_ms, "algorithmic_bytes": alg,
                          "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu,
@@ -512,7 +521,7 @@ def run_ours(args, name, w, lengths):
                     "ms_per_step": e2e_ms, "tokens_per_s": B / (e2e_ms * 1e-3),
                     "h2d_bytes_per_step": h_in.numel() * h_in.element_size(),
                     "d2h_bytes_per_step": h_out[0].numel() * h_out[0].element_size(),
-                    "path": "PagedKVLayerCache.append_rotary + .decode (ctypes C ABI), eager; "
+                    "path": "PagedKVLayerCache.rope_append_decode (ctypes C ABI), eager; "
                             "pinned host in/out, copies on a second stream overlapping compute"},
             "gpu_launches": 3 * args.steps,
             "clocks": clocks,

@@ -235,6 +235,7 @@ def rope_append_decode(
     q_out: torch.Tensor | None = None,
     workspace: DecodeWorkspace | None = None,
     status: torch.Tensor | None = None,
+    events=None,
 ) -> torch.Tensor:
     """One fused decode-attention step (``llmc_rope_append_decode``).
 
@@ -243,6 +244,7 @@ def rope_append_decode(
     ``seq_lens[b] + 1`` tokens run in one decode launch plus the merge launch, which
     also advances ``seq_lens``.  ``host_lens`` are the lengths BEFORE the step.
     Returns ``out`` shaped like ``q``; the rotated query goes to ``q_out``.
+    ``events``: optional CUDA-event pair recorded around the step's launches.
     """
     lib = N.load()
     if not q.is_cuda:
@@ -272,12 +274,16 @@ def rope_append_decode(
     max_parts = -(-(max_pages * P) // partition_tokens)
     part_o, part_lse = ws.get(B, Hq, d, max_parts)
     st = status if status is not None else default_status(q.device)
+    if events is not None:
+        events[0].record()
     rc = lib.llmc_rope_append_decode(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), q_out.data_ptr(), key_pages.data_ptr(),
         value_pages.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(), cos.data_ptr(),
         sin.data_ptr(), cos.shape[0], out.data_ptr(), N.ptr(part_o), N.ptr(part_lse),
         ws.lens_next(B).data_ptr(), st.data_ptr(), B, Hq, Hkv, d, P, max_pages, num_pages,
         partition_tokens, float(scale), N.dtype_code(q.dtype), N.stream_handle(q.device))
+    if events is not None:   # brackets the decode and merge launches of the step
+        events[1].record()
     N.check(rc, "llmc_rope_append_decode")
     return out.view(q_shape)
 

@@ -264,8 +264,9 @@ class Llama3DecodeModel:
             if self.attn_core is not None:
                 attn = self.attn_core(li, q, k, v, lc)
             else:
-                q_rot = lc.append_rotary(q, k, v, self.rope)  # fused RoPE + page append
-                attn = lc.decode(q_rot, partition_tokens=partition_tokens)
+                # RoPE + page append + paged attention in one fused decode launch
+                attn = lc.rope_append_decode(q, k, v, self.rope,
+                                             partition_tokens=partition_tokens)
             attn = attn.reshape(B, 1, self.hq * cfg.head_dim)
             o = self.tp.all_reduce_(F.linear(attn, L["wo"]))
             x, h = self._add_norm(x, L["post_norm"], o)
