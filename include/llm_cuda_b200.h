@@ -203,6 +203,23 @@ LLMC_API int llmc_add_rmsnorm(void* x, const void* delta, const void* weight, vo
 LLMC_API int llmc_swiglu(const void* gate_up, void* out, int rows, int inter, int dtype,
                          llmc_stream_t stream);
 
+/*
+ * Decode GEMM on the tcgen05 tensor cores: y[Mb, N] = x[Mb, K] . W[N, K]^T (bf16 in,
+ * fp32 accumulate in TMEM, bf16 out), Mb <= 256, N % 128 == 0, K % 64 == 0.
+ * Replaces the dense projections of a decode step (nn.Linear / Column- and
+ * RowParallelLinear, src/llm_cuda/parallel/tensor_parallel.py:44-49,83-90, and
+ * lm_head, src/llm_cuda/models/llama3/model.py:156) at decode batch sizes, where the
+ * weights are streamed once.  Persistent stream-K: every CTA takes an equal range of
+ * (128-row tile, k-chunk) work; a tile shared by several CTAs is summed from their
+ * fp32 parts in `workspace` (llmc_decode_gemm_workspace_bytes) by the last CTA to
+ * finish, which `counters` (int32 [N / 128], all zero before the first call, left
+ * zero by every call) identifies.
+ */
+LLMC_API size_t llmc_decode_gemm_workspace_bytes(int Mb, int N, int K);
+LLMC_API int llmc_decode_gemm(const void* x, const void* w, void* y, float* workspace,
+                              size_t workspace_bytes, int32_t* counters, int Mb, int N, int K,
+                              int32_t* status, llmc_stream_t stream);
+
 /* Message of the last failed call on this host thread ("" if none). */
 LLMC_API const char* llmc_last_error_string(void);
 

@@ -28,6 +28,10 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
                                 int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
                                 int D, int P, int max_pages, int num_pages, int Tpart,
                                 float scale, int dtype, std::string* err, cudaStream_t stream);
+cudaError_t launch_decode_gemm(const void* x, const void* w, void* y, float* ws, size_t ws_floats,
+                               int32_t* counters, int Mb, int N, int K, int32_t* status,
+                               std::string* err, cudaStream_t stream);
+size_t decode_gemm_workspace_floats(int Mb, int N, int K);
 cudaError_t launch_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int rows,
                                int hidden, float eps, int dtype, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dtype,
@@ -201,6 +205,30 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
                           partition_tokens, dtype, stream);
   }
   if (e != cudaSuccess) return cuda_fail(e, "llmc_rope_append_decode", err);
+  return LLMC_OK;
+}
+
+size_t llmc_decode_gemm_workspace_bytes(int Mb, int N, int K) {
+  if (Mb <= 0 || Mb > 256 || N <= 0 || K <= 0 || N % 128 || K % 64) return 0;
+  return llmc::decode_gemm_workspace_floats(Mb, N, K) * sizeof(float);
+}
+
+int llmc_decode_gemm(const void* x, const void* w, void* y, float* workspace,
+                     size_t workspace_bytes, int32_t* counters, int Mb, int N, int K,
+                     int32_t* status, llmc_stream_t stream) {
+  g_last_error.clear();
+  if (Mb <= 0 || Mb > 256 || N <= 0 || K <= 0)
+    return fail(LLMC_EINVAL, "llmc_decode_gemm: need 1 <= Mb <= 256 and positive N, K");
+  if (N % 128 || K % 64)
+    return fail(LLMC_EUNSUPPORTED, "llmc_decode_gemm: N must be a multiple of 128, K of 64");
+  if (!x || !w || !y || !workspace || !counters || !status)
+    return fail(LLMC_EINVAL, "llmc_decode_gemm: NULL pointer");
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(x) || !al(w)) return fail(LLMC_EINVAL, "llmc_decode_gemm: x and W must be 16-byte aligned");
+  std::string err;
+  cudaError_t e = llmc::launch_decode_gemm(x, w, y, workspace, workspace_bytes / sizeof(float),
+                                           counters, Mb, N, K, status, &err, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_decode_gemm", err);
   return LLMC_OK;
 }
 

@@ -1,4 +1,5 @@
-"""Fused residual-add + RMSNorm and SwiGLU kernels for the decode step (CUDA).
+"""Decode-step kernels around the attention path (CUDA): tcgen05 decode GEMM,
+fused residual-add + RMSNorm, SwiGLU.
 
 ``add_rmsnorm`` replaces the residual add (``src/llm_cuda/models/llama3/model.py:37,42``
 of llm-cuda) plus ``RMSNorm.forward`` (``norm.py:31-33``); ``swiglu`` replaces
@@ -44,3 +45,40 @@ def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
                               N.dtype_code(gate_up.dtype), N.stream_handle(gate_up.device))
     N.check(rc, "llmc_swiglu")
     return out
+
+
+_gemm_ws: dict = {}
+
+
+def _gemm_workspace(device: torch.device, Mb: int, n_out: int, k: int):
+    """fp32 partial slots + int32 counters (kept zero by the kernel) for one shape."""
+    key = (device.index, Mb, n_out, k)
+    ws = _gemm_ws.get(key)
+    if ws is None:
+        nbytes = N.load().llmc_decode_gemm_workspace_bytes(Mb, n_out, k)
+        ws = (torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=device),
+              torch.zeros(n_out // 128, dtype=torch.int32, device=device))
+        _gemm_ws[key] = ws
+    return ws
+
+
+def decode_gemm(x: torch.Tensor, w: torch.Tensor, status: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``y = x @ w.T`` on the tcgen05 tensor cores for decode batches (bf16, rows of
+    ``x`` <= 256, ``w`` [N, K] with N % 128 == 0 and K % 64 == 0)."""
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("decode_gemm takes bf16 x and W")
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K).contiguous()
+    Mb, n_out = x2.shape[0], w.shape[0]
+    y = torch.empty(Mb, n_out, dtype=torch.bfloat16, device=x.device) if out is None else out
+    ws, cnt = _gemm_workspace(x.device, Mb, n_out, K)
+    if status is None:
+        from .decode_attention import default_status
+
+        status = default_status(x.device)
+    rc = N.load().llmc_decode_gemm(x2.data_ptr(), w.data_ptr(), y.data_ptr(), ws.data_ptr(),
+                                   ws.numel() * 4, cnt.data_ptr(), Mb, n_out, K, status.data_ptr(),
+                                   N.stream_handle(x.device))
+    N.check(rc, "llmc_decode_gemm")
+    return y.view(*x.shape[:-1], n_out)

@@ -31,7 +31,7 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from ...kernels.step_ops import add_rmsnorm, swiglu
+from ...kernels.step_ops import add_rmsnorm, decode_gemm, swiglu
 from .kv_cache import PagedKVCache, make_block_table
 from .rotary import RopeTable
 
@@ -213,6 +213,15 @@ class Llama3DecodeModel:
             h = (gate * torch.sigmoid(gate)) * up         # swiglu.py:103-107
         return self.tp.all_reduce_(F.linear(h, L["wdown"]))
 
+    def _lm_head(self, h: torch.Tensor) -> torch.Tensor:
+        """Vocabulary projection.  At decode batch sizes the 1 GB bf16 weight streams
+        through the tcgen05 decode GEMM (persistent stream-K, TMEM accumulators), which
+        is faster than cuBLAS on this shape; other dtypes/shapes use F.linear."""
+        if (h.is_cuda and h.dtype == torch.bfloat16 and h.shape[0] <= 256
+                and self.lm_head.shape[0] % 128 == 0 and h.shape[-1] % 64 == 0):
+            return decode_gemm(h, self.lm_head)
+        return F.linear(h, self.lm_head)
+
     def _add_norm(self, x: torch.Tensor, w: torch.Tensor, delta: torch.Tensor | None):
         """Residual add (model.py:37,42) + RMSNorm (norm.py:31-33): returns ``(x, h)``.
         On CUDA one fused kernel updates ``x`` in place; the CPU branch serves only the
@@ -272,7 +281,7 @@ class Llama3DecodeModel:
             x, h = self._add_norm(x, L["post_norm"], o)
             delta = self._mlp(L, h)
         x, h = self._add_norm(x, self.final_norm, delta)
-        return F.linear(h[:, 0], self.lm_head)
+        return self._lm_head(h[:, 0])
 
     def bytes_per_step(self, cache: PagedKVCache) -> tuple[int, int]:
         """(weight bytes, KV bytes) this rank reads in one decode step at the current
