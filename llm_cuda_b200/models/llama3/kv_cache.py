@@ -248,3 +248,57 @@ class PagedKVCache:
 
     def check_status(self) -> None:
         self.layer_caches[0].check_status()
+
+
+class GraphedDecodeStep:
+    """The fused decode-attention step of one cache, captured once as a CUDA graph.
+
+    ``q``/``k``/``v`` are device input buffers (``[B, Hq|Hkv, 1, d]``) that the caller
+    refills before each ``replay()``; the step rotates, appends at ``seq_lens`` and
+    attends, advancing the lengths on the device and in ``cache.host_lengths``.  One
+    graph launch per step instead of several Python-issued launches: the host cost of
+    a step is that of ``cudaGraphLaunch``.  ``partition_tokens`` is fixed at capture.
+    """
+
+    def __init__(self, cache: PagedKVLayerCache, rope: RopeTable, q: torch.Tensor,
+                 k: torch.Tensor, v: torch.Tensor, partition_tokens: int | None = None,
+                 out: torch.Tensor | None = None):
+        from ...kernels.decode_attention import choose_partition_tokens, _num_sms
+
+        self.cache, self.rope, self.q, self.k, self.v = cache, rope, q, k, v
+        B, Hq, d = q.shape[0], q.shape[1], q.shape[-1]
+        if partition_tokens is None:
+            partition_tokens = choose_partition_tokens(
+                [x + 1 for x in cache.host_lengths], cache.num_kv_heads, Hq // cache.num_kv_heads,
+                _num_sms(q.device), max_tokens=cache.max_pages * cache.page_size)
+        self.partition_tokens = partition_tokens
+        self.out = out if out is not None else torch.empty(B, Hq, d, dtype=q.dtype,
+                                                           device=q.device)
+        self.q_rot = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device)
+        lens0 = cache.seq_lens.clone()
+        host0 = list(cache.host_lengths)
+        self._step()                          # warm-up: workspaces exist before capture
+        torch.cuda.synchronize(q.device)
+        cache.seq_lens.copy_(lens0)
+        s = torch.cuda.Stream(device=q.device)
+        s.wait_stream(torch.cuda.current_stream(q.device))
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(self.graph, stream=s):
+                self._step()
+        torch.cuda.current_stream(q.device).wait_stream(s)
+        torch.cuda.synchronize(q.device)
+        cache.seq_lens.copy_(lens0)
+        cache.host_lengths = host0
+
+    def _step(self):
+        c = self.cache
+        rope_append_decode(self.q, self.k, self.v, c.key_pages, c.value_pages, c.block_table,
+                           c.seq_lens, self.rope.cos, self.rope.sin,
+                           partition_tokens=self.partition_tokens, out=self.out,
+                           q_out=self.q_rot, workspace=c.workspace, status=c.status)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        self.cache.advance_host_lengths(1)
+        return self.out

@@ -412,3 +412,39 @@ def test_fused_step_graph_replay():
     cache.check_status()
     assert torch.equal(out.view_as(eager), eager)
     assert cache.seq_lens.tolist() == [L + 1 for L in lens]
+
+
+def test_graphed_decode_step_matches_eager_two_steps():
+    from llm_cuda_b200.models.llama3.kv_cache import GraphedDecodeStep
+
+    B, Hq, Hkv, d, P = 6, 32, 8, 128, 16
+    lens = [100 + 50 * i for i in range(B)]
+    cache, _ = _random_paged(B, Hq, Hkv, d, [L + 8 for L in lens], P, torch.bfloat16, 2012)
+    rope = RopeTable(cache.max_seq_len, d, C.THETA, DEV, torch.bfloat16)
+    gd = torch.Generator(device=DEV).manual_seed(9)
+    qs = [torch.randn(B, Hq, 1, d, device=DEV, generator=gd).bfloat16() for _ in range(2)]
+    ks = [torch.randn(B, Hkv, 1, d, device=DEV, generator=gd).bfloat16() for _ in range(2)]
+    vs = [torch.randn(B, Hkv, 1, d, device=DEV, generator=gd).bfloat16() for _ in range(2)]
+    kp0, vp0 = cache.key_pages.clone(), cache.value_pages.clone()
+
+    def reset():
+        cache.key_pages.copy_(kp0)
+        cache.value_pages.copy_(vp0)
+        cache.seq_lens.copy_(torch.tensor(lens, dtype=torch.int32))
+        cache.host_lengths = list(lens)
+
+    reset()
+    eager = [cache.rope_append_decode(qs[i], ks[i], vs[i], rope, partition_tokens=128).clone()
+             for i in range(2)]
+    reset()
+    qb, kb, vb = torch.empty_like(qs[0]), torch.empty_like(ks[0]), torch.empty_like(vs[0])
+    step = GraphedDecodeStep(cache, rope, qb, kb, vb, partition_tokens=128)
+    for i in range(2):
+        qb.copy_(qs[i])
+        kb.copy_(ks[i])
+        vb.copy_(vs[i])
+        out = step.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out.view_as(eager[i]), eager[i])
+    cache.check_status()
+    assert cache.seq_lens.tolist() == [L + 2 for L in lens] and cache.host_lengths == [L + 2 for L in lens]
