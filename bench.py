@@ -308,10 +308,34 @@ def triton_reference_compare(sets, lengths) -> dict:
             "max_abs_diff_vs_ours": (out_ref[:, :, 0].float() - ours).abs().max().item()}
 
 
+def _balanced_partials(lengths, hkv: int, group: int, grid: int) -> int:
+    """Split-K partials (one per query head and segment) that the balanced split writes
+    and the merge reads back: rows (sequence, KV head, head group) of ceil(L/64)
+    chunks laid end to end, CTA c taking chunks [c*total/grid, (c+1)*total/grid)."""
+    hg = (group + 7) // 8
+    chunks = [(L + 63) // 64 for L in lengths for _ in range(hkv * hg)]
+    heads = [min(8, group - 8 * j) for _ in lengths for _ in range(hkv) for j in range(hg)]
+    total = sum(chunks)
+    if total == 0:
+        return 0
+
+    def owner(x):
+        return ((x + 1) * grid + total - 1) // total - 1
+
+    n, x0 = 0, 0
+    for c, h in zip(chunks, heads):
+        if c:
+            segs = owner(x0 + c - 1) - owner(x0) + 1
+            if segs > 1:
+                n += segs * h
+        x0 += c
+    return n
+
+
 def run_ours(args, name, w, lengths):
     from llm_cuda_b200 import _native as N
     from llm_cuda_b200.kernels.decode_attention import (
-        choose_partition_tokens, paged_decode, rope_append_decode)
+        BALANCED, paged_decode, rope_append_decode)
     from llm_cuda_b200.models.llama3 import PagedKVLayerCache, RopeTable, make_block_table
     from llm_cuda_b200.models.llama3.kv_cache import GraphedDecodeStep
 
@@ -328,7 +352,9 @@ def run_ours(args, name, w, lengths):
     kv_bytes_rank = sum(lengths) * hkv * d * 2 * 2    # K and V read per step
     n_sets = max(1, math.ceil(3 * L2_BYTES / kv_bytes_rank)) if kv_bytes_rank < 3 * L2_BYTES else 1
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    T = w["part"] or choose_partition_tokens(lengths, hkv, hq // hkv, sms, max_pages * P)
+    # Configs 2/3: the balanced split (equal chunk ranges per SM, computed on the
+    # device); config 4 names its 4096-token partitions.
+    T = w["part"] or BALANCED
 
     gen = torch.Generator().manual_seed(w["seed"] + 7919 * rank)
     gd = torch.Generator(device=dev).manual_seed(w["seed"] + rank)
@@ -495,9 +521,12 @@ def run_ours(args, name, w, lengths):
     # algorithmic bytes of the fused decode launch + its merge launch on one rank: K/V
     # of the whole context, raw q in, rotated q and out written, the new token's k/v
     # read and appended, block table, split-K partials written and read back
-    parts = sum(math.ceil(L / T) for L in lengths) if max(lengths) > T else 0
+    if T == BALANCED:
+        parts = _balanced_partials(lengths, hkv, hq // hkv, sms)
+    else:   # partitions of split sequences, one partial per query head each
+        parts = sum(math.ceil(L / T) for L in lengths if L > T) * hq
     alg = (kv_bytes_rank + 3 * B * hq * d * 2 + 2 * 2 * B * hkv * d * 2 + sum(pages_per) * 4
-           + B * 4 + 2 * parts * hq * (d + 1) * 4)
+           + B * 4 + 2 * parts * (d + 1) * 4)
     achieved = alg / (k_ms * 1e-3) / 1e9
     peaks = _peaks()
     if rank == 0:
@@ -511,7 +540,8 @@ def run_ours(args, name, w, lengths):
             "hbm_frac_step": value / world / peaks["hbm_gbs"],
             "config": {"workload": w["desc"], "B": B, "Hq": Hq, "Hkv": Hkv, "head_dim": d,
                        "page_size": P, "context_tokens_total": sum(lengths),
-                       "partition_tokens": T, "parallelism": f"tp{world} (KV-head sharded)",
+                       "partition_tokens": T if T else "balanced",
+                       "parallelism": f"tp{world} (KV-head sharded)",
                        "input_sets": n_sets,
                        "l2": f"KV per rank {kv_bytes_rank / 1e6:.0f} MB x {n_sets} rotating sets "
                              f"> L2 126 MB (no flush needed)",
@@ -548,7 +578,7 @@ def run_c5(args):
     all-reduce after o_proj and down_proj; K timed greedy decode steps, each replayed
     from one CUDA graph of the whole step."""
     from llm_cuda_b200 import _native as N
-    from llm_cuda_b200.kernels.decode_attention import choose_partition_tokens
+    from llm_cuda_b200.kernels.decode_attention import BALANCED
     from llm_cuda_b200.models.llama3.decode_model import (
         DecodeConfig, DecodeGraph, Llama3DecodeModel, TensorParallel)
 
@@ -567,9 +597,7 @@ def run_c5(args):
     with torch.no_grad():
         first = model.prefill(ids, cache).argmax(-1)
     torch.cuda.synchronize()
-    sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    T = choose_partition_tokens([prompt + steps] * B, model.hkv, model.hq // model.hkv, sms,
-                                cap)
+    T = BALANCED   # the captured step re-balances on the device as contexts grow
     graph = DecodeGraph(model, cache, first, partition_tokens=T)
     lens0 = cache.get_layer(0).seq_lens.clone()
 
@@ -641,7 +669,7 @@ def run_c5(args):
                                    "to 2048 (page 16), greedy decode",
                        "parallelism": f"tp{world} (head-sharded, NCCL all-reduce after "
                                       "o_proj/down_proj)",
-                       "partition_tokens": T, "graph": "whole step (32 layers + lm_head + "
+                       "partition_tokens": "balanced", "graph": "whole step (32 layers + lm_head + "
                                                        "argmax) replayed from one CUDA graph",
                        "weight_bytes_per_rank": w_bytes,
                        "kv_bytes_per_rank_per_step_avg": kv_total / steps},

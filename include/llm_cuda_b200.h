@@ -93,6 +93,38 @@ LLMC_API size_t llmc_decode_partials_bytes(int B, int Hq, int d, int max_parts, 
 LLMC_API int llmc_num_partitions(int max_tokens, int partition_tokens);
 
 /*
+ * partition_tokens == LLMC_PARTITION_BALANCED selects the balanced split of the TMA
+ * kernel.  It has no counterpart in the reference, which has no split-K.
+ *  - The 64-token chunks of all (sequence, KV head) rows are laid end to end, and
+ *    CTA c of the G = SM-count grid takes chunks [c*total/G, (c+1)*total/G).
+ *  - Every SM gets the same number of tokens whatever the lengths. The split is
+ *    computed on the device from seq_lens, so a captured graph stays balanced as
+ *    contexts grow.
+ *  - Rows that one CTA covers entirely go straight to out. The others leave one
+ *    partial per CTA, and the CTA that completes a row's last partial merges the row.
+ *    The decode launch thus finishes out by itself, and llmc_lse_merge with
+ *    partition_tokens 0 does nothing.
+ *  - The partials buffers are sized by llmc_balanced_partials_bytes on the device that
+ *    runs the kernels.
+ *  - part_lse begins with counter words, one per row plus one. These must be zero
+ *    before a call: zero the buffer when it is allocated, when (B, Hq, Hkv) changes,
+ *    and after a call that reported LLMC_STATUS_WAIT_TIMEOUT. Every completed call
+ *    leaves them at zero.
+ *  - llmc_paged_decode returns LLMC_EUNSUPPORTED where the TMA kernel does not apply
+ *    (see llmc_decode_balanced_supported). llmc_rope_append_decode then falls back to
+ *    uniform partitions that fit the same buffers.
+ */
+#define LLMC_PARTITION_BALANCED 0
+
+/* Bytes of part_o (returned) and part_lse (*lse_bytes) for the balanced split. */
+LLMC_API size_t llmc_balanced_partials_bytes(int B, int Hq, int Hkv, int d, size_t* lse_bytes);
+
+/* 1 if llmc_paged_decode takes LLMC_PARTITION_BALANCED for these arguments, else 0. */
+LLMC_API int llmc_decode_balanced_supported(const void* q, const void* k_pages,
+                                            const void* v_pages, int dtype, int d,
+                                            int page_size, int max_pages_per_seq, int B);
+
+/*
  * Paged GQA flash-decode: one query token per sequence against its paged K/V.
  *
  * Replaces triton_decode_attention / _decode_attention_kernel
@@ -105,7 +137,8 @@ LLMC_API int llmc_num_partitions(int max_tokens, int partition_tokens);
  *   q   [B, Hq, d]; out [B, Hq, d] (same dtype)
  *   k_pages, v_pages [num_pages, Hkv, page_size, d]
  *   block_table [B, max_pages_per_seq] int32; seq_lens [B] int32 (tokens to attend)
- *   partition_tokens: split-K bound T (multiple of 64).  A context of L tokens is cut
+ *   partition_tokens: split-K bound T (multiple of 64), or LLMC_PARTITION_BALANCED.
+ *     With T > 0 a context of L tokens is cut
  *     into n = ceil(L / T) partitions of equal length (L / n rounded up to 64).
  *     Sequences with n > 1 leave normalised partials + log2-sum-exp in part_o/part_lse
  *     for llmc_lse_merge; single-partition sequences are written to out directly.
@@ -137,7 +170,9 @@ LLMC_API int llmc_paged_decode(const void* q, const void* k_pages, const void* v
  *   seq_lens [B]: lengths BEFORE the step; the new token goes to position seq_lens[b]
  *     and on completion seq_lens[b] has grown by one (written by the merge launch).
  *   q_rot_out [B, Hq, d]: receives the rotated query (required).
- *   lens_next [B] int32 scratch.  Other arguments as llmc_rope_append / llmc_paged_decode.
+ *   lens_next [B] int32 scratch (not used by the balanced split, which publishes the
+ *     lengths from inside the decode launch).  Other arguments as llmc_rope_append /
+ *     llmc_paged_decode.
  * In the fused kernel every CTA rotates its query fragments in registers and the warp
  * whose tile holds the new token rotates k and patches k/v into the landed tile and
  * the page.  Shapes the fused kernel does not take run the three separate kernels.

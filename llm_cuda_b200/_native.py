@@ -34,6 +34,8 @@ SIGNATURES = {
     "llmc_rope_append": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P] + [_I] * 10 + [_P, _P]),
     "llmc_decode_partials_bytes": (_SZ, [_I, _I, _I, _I, ctypes.POINTER(_SZ)]),
     "llmc_num_partitions": (_I, [_I, _I]),
+    "llmc_balanced_partials_bytes": (_SZ, [_I, _I, _I, _I, ctypes.POINTER(_SZ)]),
+    "llmc_decode_balanced_supported": (_I, [_P, _P, _P] + [_I] * 5),
     "llmc_paged_decode": (_I, [_P] * 9 + [_I] * 8 + [_F, _I, _I, _P]),
     "llmc_lse_merge": (_I, [_P, _P, _P, _P] + [_I] * 6 + [_P]),
     "llmc_paged_decode_noalloc": (_I, [_P] * 7 + [_I] * 8 + [_F, _I, _P]),

@@ -32,6 +32,9 @@ cudaError_t launch_decode_gemm(const void* x, const void* w, void* y, float* ws,
                                int32_t* counters, int Mb, int N, int K, int32_t* status,
                                std::string* err, cudaStream_t stream);
 size_t decode_gemm_workspace_floats(int Mb, int N, int K);
+int balanced_grid();
+bool fast_path_applies(int dtype, int D, int P, int max_pages, int Tpart, int B,
+                       const void* q, const void* kp, const void* vp);
 cudaError_t launch_add_rmsnorm(void* x, const void* delta, const void* w, void* h, int rows,
                                int hidden, float eps, int dtype, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dtype,
@@ -77,6 +80,25 @@ size_t llmc_decode_partials_bytes(int B, int Hq, int d, int max_parts, size_t* l
   return rows * (size_t)(d > 0 ? d : 0) * sizeof(float);
 }
 
+size_t llmc_balanced_partials_bytes(int B, int Hq, int Hkv, int d, size_t* lse_bytes) {
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || d <= 0) {
+    if (lse_bytes) *lse_bytes = 0;
+    return 0;
+  }
+  const size_t rows = (size_t)B * Hkv * ((Hq / Hkv + 7) / 8);
+  const size_t slots = rows + (size_t)llmc::balanced_grid();
+  const size_t counters = (size_t)llmc::balanced_counter_words((int)rows);
+  if (lse_bytes) *lse_bytes = (counters + slots * 8) * sizeof(float);
+  return slots * 8 * (size_t)d * sizeof(float);
+}
+
+int llmc_decode_balanced_supported(const void* q, const void* k_pages, const void* v_pages,
+                                   int dtype, int d, int page_size, int max_pages_per_seq,
+                                   int B) {
+  return llmc::fast_path_applies(dtype, d, page_size, max_pages_per_seq, 0, B, q, k_pages,
+                                 v_pages) ? 1 : 0;
+}
+
 int llmc_rope_append(const void* q_in, const void* k_in, const void* v_in, void* q_out,
                      void* k_pages, void* v_pages, const int32_t* block_table, int32_t* seq_lens,
                      const void* cos_tab, const void* sin_tab, int B, int S, int Hq, int Hkv,
@@ -114,7 +136,7 @@ int llmc_paged_decode(const void* q, const void* k_pages, const void* v_pages,
   g_last_error.clear();
   if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_paged_decode: unknown dtype");
   if (B < 0 || Hq <= 0 || Hkv <= 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
-      num_pages <= 0 || partition_tokens <= 0)
+      num_pages <= 0 || partition_tokens < 0)
     return fail(LLMC_EINVAL, "llmc_paged_decode: sizes must be positive");
   if (Hq % Hkv) return fail(LLMC_EINVAL, "llmc_paged_decode: Hq must be a multiple of Hkv");
   if (d > 256) return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode: head_dim > 256");
@@ -127,7 +149,7 @@ int llmc_paged_decode(const void* q, const void* k_pages, const void* v_pages,
   if (!q || !k_pages || !v_pages || !block_table || !seq_lens || !out || !status)
     return fail(LLMC_EINVAL, "llmc_paged_decode: NULL pointer argument");
   const int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
-  if (max_parts > 1 && (!part_o || !part_lse))
+  if ((partition_tokens == 0 || max_parts > 1) && (!part_o || !part_lse))
     return fail(LLMC_EINVAL,
                 "llmc_paged_decode: part_o/part_lse are required when a sequence can span "
                 "more than one partition");
@@ -136,6 +158,8 @@ int llmc_paged_decode(const void* q, const void* k_pages, const void* v_pages,
                                             part_o, part_lse, status, B, Hq, Hkv, d, page_size,
                                             max_pages_per_seq, num_pages, partition_tokens, scale,
                                             dtype, flags, &err, (cudaStream_t)stream);
+  if (e == cudaErrorNotSupported && partition_tokens == 0)
+    return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode: " + err);
   if (e != cudaSuccess) return cuda_fail(e, "llmc_paged_decode", err);
   return LLMC_OK;
 }
@@ -145,10 +169,11 @@ int llmc_lse_merge(const float* part_o, const float* part_lse, const int32_t* se
                    llmc_stream_t stream) {
   g_last_error.clear();
   if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_lse_merge: unknown dtype");
-  if (B < 0 || Hq <= 0 || d <= 0 || max_parts <= 0 || partition_tokens <= 0)
+  if (B < 0 || Hq <= 0 || d <= 0 || partition_tokens < 0 ||
+      (partition_tokens > 0 && max_parts <= 0))
     return fail(LLMC_EINVAL, "llmc_lse_merge: sizes must be positive");
   if (!seq_lens || !out) return fail(LLMC_EINVAL, "llmc_lse_merge: NULL pointer argument");
-  if (max_parts > 1 && (!part_o || !part_lse))
+  if ((partition_tokens == 0 || max_parts > 1) && (!part_o || !part_lse))
     return fail(LLMC_EINVAL, "llmc_lse_merge: NULL partials with max_parts > 1");
   cudaError_t e = llmc::launch_lse_merge(part_o, part_lse, seq_lens, out, B, Hq, d, max_parts,
                                          partition_tokens, max_parts * partition_tokens, dtype,
@@ -167,7 +192,7 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
   g_last_error.clear();
   if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_rope_append_decode: unknown dtype");
   if (B < 0 || Hq <= 0 || Hkv <= 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
-      num_pages <= 0 || partition_tokens <= 0 || rope_max_pos <= 0)
+      num_pages <= 0 || partition_tokens < 0 || rope_max_pos <= 0)
     return fail(LLMC_EINVAL, "llmc_rope_append_decode: sizes must be positive");
   if (Hq % Hkv) return fail(LLMC_EINVAL, "llmc_rope_append_decode: Hq must be a multiple of Hkv");
   if (d % 2 || d > 256)
@@ -181,8 +206,8 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
   if (!q || !k_new || !v_new || !q_rot_out || !k_pages || !v_pages || !block_table || !seq_lens ||
       !cos_tab || !sin_tab || !out || !lens_next || !status)
     return fail(LLMC_EINVAL, "llmc_rope_append_decode: NULL pointer argument");
-  const int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
-  if (max_parts > 1 && (!part_o || !part_lse))
+  int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
+  if ((partition_tokens == 0 || max_parts > 1) && (!part_o || !part_lse))
     return fail(LLMC_EINVAL, "llmc_rope_append_decode: part_o/part_lse are required");
   if (B == 0) return LLMC_OK;
   std::string err;
@@ -193,6 +218,22 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
   if (e == cudaErrorNotSupported) {
     // Shape outside the fused kernel: the same step with the separate kernels.
     cudaGetLastError();
+    if (partition_tokens == 0) {
+      // The balanced split needs the fused kernel; the SIMT kernel gets uniform
+      // partitions, as many as the balanced workspace holds.
+      size_t lse_b = 0;
+      const size_t o_b = llmc_balanced_partials_bytes(B, Hq, Hkv, d, &lse_b);
+      size_t per_part = 0;
+      const size_t o1 = llmc_decode_partials_bytes(B, Hq, d, 1, &per_part);
+      size_t fit = o1 ? o_b / o1 : 1;
+      if (per_part && lse_b / per_part < fit) fit = lse_b / per_part;
+      if (fit < 1) fit = 1;
+      const long long cap = (long long)max_pages_per_seq * page_size;
+      long long T = (cap + (long long)fit - 1) / (long long)fit;
+      T = (T + 63) / 64 * 64;
+      partition_tokens = (int)(T < (1ll << 30) ? T : (1ll << 30));
+      max_parts = llmc_num_partitions((int)cap, partition_tokens);
+    }
     int rc = llmc_rope_append(q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens,
                               cos_tab, sin_tab, B, 1, Hq, Hkv, d, page_size, max_pages_per_seq,
                               num_pages, rope_max_pos, dtype, status, stream);

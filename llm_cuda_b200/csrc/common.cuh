@@ -15,6 +15,13 @@
 
 namespace llmc {
 
+// Counter words at the head of the balanced split's part_lse buffer: one per row
+// (sequence, KV head, head group) plus a CTA counter, padded to 128 bytes.
+__host__ __device__ __forceinline__ int balanced_counter_words(int rows) {
+  return ((rows + 1) + 31) & ~31;
+}
+
+
 // Status bits written (atomicOr) into the caller's device status word.  The
 // host reads the word after synchronising and raises; kernels never trap.
 enum StatusBits : int {

@@ -54,7 +54,10 @@ constexpr int kStageTok = 64;          // tokens per pipeline stage
 constexpr int kGroups = 3;
 constexpr int kWarpsPerGroup = 2;
 constexpr int kConsumers = kGroups * kWarpsPerGroup;
-constexpr int kThreads = (kConsumers + 1) * 32;
+// Warp kConsumers is the TMA producer; warp kMergeWarp (balanced split only)
+// publishes split segments and merges completed rows off the streaming path.
+constexpr int kMergeWarp = kConsumers + 1;
+constexpr int kThreads = (kConsumers + 2) * 32;
 constexpr int kMaxStages = 12;
 constexpr int kRowBytes = 128;         // one swizzle row = 64 bf16/fp16 elements
 
@@ -82,6 +85,18 @@ struct Params {
   void* q_rot_out;         // [B, Hq, D] rotated query (written once per head)
   int32_t* lens_next;      // [B]
   int rope_max_pos;
+  // Balanced split (partition_tokens == 0): every CTA takes an equal contiguous range
+  // of the 64-token chunks of all rows (sequence, KV head, head group) in order, cut
+  // into pieces of at most cap_chunks chunks.  The part of a row that one CTA covers
+  // is a segment: its partial goes to slot (row + CTA index), unique over all
+  // segments.  The CTA that completes a row's last segment merges the row
+  // (counters[row] counts finished segments); counters[rows] counts CTAs past their
+  // length reads, and the last of them publishes the grown lengths (FUSE).  Every
+  // counter is returned to zero by the CTA that completes it.
+  int balanced;
+  int cap_chunks;
+  int32_t* counters;       // [rows + 1], zero between calls
+  int32_t* seq_lens_out;   // FUSE + balanced: lengths after the step are written here
 };
 
 // Byte offset of (row, 16-byte chunk) inside a 128B-swizzled region whose base is
@@ -119,6 +134,198 @@ __device__ __forceinline__ Item decode_item(int i, const int* prefix, int B, int
   return it;
 }
 
+// A piece: consecutive stages of one row that a CTA processes without a break.
+// first/last: the piece opens/closes this CTA's segment of the row (softmax state
+// is reset before the first and written out after the last); whole: the segment is
+// the entire row, so the result goes straight to `out`.  part: uniform mode, the
+// partition index; balanced mode, the partial slot.
+struct Piece {
+  int b, kvh, hg, t0, t1, L, part;
+  bool first, last, whole;
+  // Balanced, last piece of a split row's segment: CTAs cf..cl hold the row (nlive
+  // of them own chunks); total = chunks of all rows.
+  int cf, cl, nlive;
+  long long total;
+};
+
+// CTA owning chunk x when `total` chunks are cut into G equal ranges
+// [c*total/G, (c+1)*total/G): the largest c with c*total/G <= x.
+__device__ __forceinline__ int chunk_owner(long long x, long long total, int G) {
+  return (int)(((x + 1) * G + total - 1) / total) - 1;
+}
+
+// The sequence of pieces of this CTA.  Uniform mode: items blockIdx.x, +gridDim.x,
+// ... (one piece each).  Balanced mode: a walk over chunks [start, end) of the
+// flattened row space; prefix[] holds per-sequence chunk prefix sums and every row
+// of sequence b has prefix[b+1] - prefix[b] chunks.
+struct Walker {
+  const int* prefix;
+  const int* lens;
+  int B, Hkv, HG, T, cap, total_items;
+  bool balanced;
+  int i, phase;
+  long long x, start, end, p0, phase_end;
+
+  // Sequence b of flattened chunk x and the first chunk of x's row.
+  __device__ void locate(long long xx, int& b, long long& row_begin) const {
+    const int RS = Hkv * HG;
+    const long long key = xx / RS;       // prefix[b] * RS <= xx  <=>  prefix[b] <= xx / RS
+    int lo = 0, hi = B;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (prefix[mid] <= key) lo = mid; else hi = mid;
+    }
+    b = lo;
+    const int n = prefix[b + 1] - prefix[b];
+    const long long local = xx - (long long)prefix[b] * RS;
+    row_begin = xx - local % n;
+  }
+
+  __device__ void init(const Params& p, const int* pre, const int* ln) {
+    prefix = pre; lens = ln; B = p.B; Hkv = p.Hkv; HG = p.HG; T = p.T; cap = p.cap_chunks;
+    balanced = p.balanced != 0;
+    total_items = prefix[B];
+    i = blockIdx.x;
+    const long long total = (long long)prefix[B] * Hkv * HG;
+    start = (long long)blockIdx.x * total / gridDim.x;
+    end = ((long long)blockIdx.x + 1) * total / gridDim.x;
+    // The range's last segment (usually the head of a row that the next CTA
+    // continues) goes first, then the range from its start: both segments a CTA
+    // shares with its neighbours finish early, so the row merges they trigger run
+    // while the other CTAs are still streaming rather than at the end.
+    p0 = start;
+    if (balanced && end > start) {
+      int b;
+      long long rb;
+      locate(end - 1, b, rb);
+      p0 = rb > start ? rb : start;
+    }
+    phase = 0;
+    x = p0;
+    phase_end = end;
+  }
+
+  __device__ bool next(Piece& pc) {
+    if (!balanced) {
+      if (i >= total_items) return false;
+      const Item it = decode_item(i, prefix, B, Hkv, HG, lens, T);
+      i += gridDim.x;
+      pc.b = it.b; pc.kvh = it.kvh; pc.hg = it.hg; pc.t0 = it.t0; pc.t1 = it.t1;
+      pc.L = it.L; pc.part = it.part;
+      pc.first = pc.last = true;
+      pc.whole = it.L <= T;
+      pc.cf = pc.cl = pc.nlive = 0;
+      pc.total = 0;
+      return true;
+    }
+    if (x >= phase_end) {
+      if (phase == 1 || p0 == start) return false;
+      phase = 1;
+      x = start;
+      phase_end = p0;
+    }
+    const int RS = Hkv * HG;
+    int b;
+    long long row_begin;
+    locate(x, b, row_begin);
+    const int n = prefix[b + 1] - prefix[b];
+    const int ri = (int)((row_begin - (long long)prefix[b] * RS) / n);
+    const int c0 = (int)(x - row_begin);
+    const long long row_end = row_begin + n;
+    long long e = phase_end < row_end ? phase_end : row_end;
+    if (e > x + cap) e = x + cap;
+    pc.b = b; pc.kvh = ri / HG; pc.hg = ri - pc.kvh * HG;
+    pc.L = lens[b];
+    pc.t0 = c0 * kStageTok;
+    pc.t1 = min(pc.L, (int)((c0 + (e - x)) * kStageTok));
+    pc.first = x == (row_begin > start ? row_begin : start);
+    pc.last = e == (row_end < end ? row_end : end);
+    pc.whole = row_begin >= start && row_end <= end;
+    pc.part = (b * Hkv + pc.kvh) * HG + pc.hg + blockIdx.x;
+    pc.cf = pc.cl = pc.nlive = 0;
+    pc.total = 0;
+    if (!pc.whole && pc.last) {   // only the segment epilogue needs them
+      const long long total = (long long)prefix[B] * RS;
+      const int G = gridDim.x;
+      pc.total = total;
+      pc.cf = chunk_owner(row_begin, total, G);
+      pc.cl = chunk_owner(row_end - 1, total, G);
+      if (total >= G) {
+        pc.nlive = pc.cl - pc.cf + 1;
+      } else {   // some CTAs own no chunk and hold no segment
+        for (int c = pc.cf; c <= pc.cl; ++c)
+          pc.nlive += ((long long)c * total / G != ((long long)c + 1) * total / G);
+      }
+    }
+    x = e;
+    return true;
+  }
+};
+
+// Log-sum-exp merge of one row's segment partials, by one warp: lane = (head hn,
+// quarter dq of head_dim).  out = sum_c 2^(lse_c - M) o_c / sum_c 2^(lse_c - M) over
+// the CTAs c in [cf, cl] that own chunks.  Partials of other CTAs are read through
+// L2 (ld.global.cg), so no stale L1 line is used.
+template <int D, typename T>
+__device__ __forceinline__ void merge_row(const Params& p, const Piece& it, int r, int hn, int dq,
+                                          int nh) {
+  if (hn >= nh) return;
+  const int G = gridDim.x;
+  const long long total = it.total;
+  auto live = [&](int cc) -> bool {
+    return cc <= it.cl &&
+           (total >= G || (long long)cc * total / G != ((long long)cc + 1) * total / G);
+  };
+  const float* lse = p.part_lse + (size_t)r * 8 + hn;
+  const float* pobase = p.part_o + ((size_t)r * 8 + hn) * D + dq;
+  const int hq = it.kvh * p.G + it.hg * 8 + hn;
+  T* orow = reinterpret_cast<T*>(p.out) + ((size_t)it.b * p.Hq + hq) * D + dq;
+  constexpr int U = 4;                       // segments whose loads are issued together
+  constexpr int DPL = D / 4;                 // head_dim values of this lane: dq + 4j
+  constexpr int CH = DPL < 16 ? DPL : 16;    // accumulated per pass
+  // Online max / sum over the segments' log2-sum-exps, U loads in flight at a time.
+  float M = -INFINITY, S = 0.f;
+  float l0[U];
+  for (int c0 = it.cf; c0 <= it.cl; c0 += U) {
+    float l[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) l[u] = live(c0 + u) ? __ldcg(lse + (size_t)(c0 + u) * 8) : -INFINITY;
+    float mb = M;
+#pragma unroll
+    for (int u = 0; u < U; ++u) mb = fmaxf(mb, l[u]);
+    S *= exp2f(M - mb);                      // M = -inf on the first batch: S = 0 anyway
+#pragma unroll
+    for (int u = 0; u < U; ++u) S += exp2f(l[u] - mb);
+    M = mb;
+    if (c0 == it.cf) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) l0[u] = l[u];
+    }
+  }
+  const float inv = 1.f / S;
+  const bool one_batch = it.cl - it.cf < U;  // weights straight from registers
+#pragma unroll 1
+  for (int j0 = 0; j0 < DPL; j0 += CH) {
+    float acc[CH];
+#pragma unroll
+    for (int j = 0; j < CH; ++j) acc[j] = 0.f;
+    for (int c0 = it.cf; c0 <= it.cl; c0 += U) {
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int cc = c0 + u;
+        if (!live(cc)) continue;
+        const float lv = one_batch ? l0[u] : __ldcg(lse + (size_t)cc * 8);
+        const float w = exp2f(lv - M) * inv;
+        const float* po = pobase + (size_t)cc * 8 * D + 4 * j0;
+#pragma unroll
+        for (int j = 0; j < CH; ++j) acc[j] = fmaf(w, __ldcg(po + 4 * j), acc[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < CH; ++j) orow[4 * (j0 + j)] = from_f32<T>(acc[j]);
+  }
+}
+
 template <int D, typename T, int ST, bool FUSE>
 __global__ void __launch_bounds__(kThreads, 1)
 paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
@@ -153,6 +360,11 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   volatile int* abort_flag = bt_s + 2 * p.max_entries;
   int* comb_count = bt_s + 2 * p.max_entries + 1;        // warps done with the current item
   volatile int* comb_done = bt_s + 2 * p.max_entries + 2; // items combined so far
+  volatile int* pend_flag = bt_s + 2 * p.max_entries + 3; // handoff slot: 1 = holds a segment
+  // Handoff slot of a split segment's combined partial, consumers -> merge warp:
+  // normalised o [8 heads][D] then log2-sum-exp [8].
+  float* pend_o = reinterpret_cast<float*>(bt_s + 2 * p.max_entries + 4);
+  float* pend_lse = pend_o + 8 * D;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -166,6 +378,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     *abort_flag = 0;
     *comb_count = 0;
     *comb_done = 0;
+    *pend_flag = 0;
     fence_mbarrier_init();
   }
   if (warp == kConsumers && lane == 0) {
@@ -192,10 +405,13 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       if (FUSE && report && L > p.rope_max_pos) atomicOr(p.status, kStatusRopeRange);
       return L;
     };
-    for (int b = lo; b < hi; ++b) {
-      const int L = eff_len(b, true);
-      sum += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
-    }
+    // Work units of sequence b: uniform mode, its items; balanced mode, the 64-token
+    // chunks of one of its rows.
+    auto units = [&](int L) -> int {
+      if (L <= 0) return 0;
+      return p.balanced ? (L + kStageTok - 1) / kStageTok : (L + p.T - 1) / p.T * per_part;
+    };
+    for (int b = lo; b < hi; ++b) sum += units(eff_len(b, true));
     int incl = sum;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -208,12 +424,74 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const int L = eff_len(b, false);
       lens[b] = L;
       if (FUSE && blockIdx.x == 0) p.lens_next[b] = L;
-      run += (L > 0 ? (L + p.T - 1) / p.T : 0) * per_part;
+      run += units(L);
     }
     if (lane == 31) prefix[p.B] = incl;
   }
   __syncthreads();
-  const int total_items = prefix[p.B];
+
+  if (warp == kMergeWarp) {
+    // ======================= merge warp =======================
+    if (!p.balanced) return;
+    const int n_rows = p.B * p.Hkv * p.HG;
+    // Empty contexts have no chunk: their rows get acc / max(l, 1e-9) = 0 here.
+    for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
+      if (lens[b] != 0) continue;
+      T* ob = reinterpret_cast<T*>(p.out) + (size_t)b * p.Hq * D;
+      for (int i = lane; i < p.Hq * D; i += 32) ob[i] = from_f32<T>(0.f);
+    }
+    if (FUSE) {
+      // Every CTA has read seq_lens (before the barrier above); the last one to get
+      // here publishes the grown lengths and re-arms the counter.
+      int last = 0;
+      if (lane == 0) last = atomicAdd(&p.counters[n_rows], 1) == (int)gridDim.x - 1;
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (last) {
+        for (int b = lane; b < p.B; b += 32) p.seq_lens_out[b] = lens[b];
+        if (lane == 0) p.counters[n_rows] = 0;
+      }
+    }
+    // Split segments arrive through the handoff slot in walk order.
+    const int hn = lane & 7, dq = lane >> 3;
+    Walker walk;
+    walk.init(p, prefix, lens);
+    Piece it;
+    while (walk.next(it)) {
+      if (!it.last || it.whole) continue;
+      {
+        const unsigned long long t0 = globaltimer_ns();
+        while (*pend_flag == 0 && !*abort_flag) {
+          if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            atomicOr(p.status, kStatusWaitTimeout);
+          }
+        }
+      }
+      if (*abort_flag) break;
+      __threadfence_block();
+      const int nh = min(8, p.G - it.hg * 8);
+      const size_t pidx = (size_t)it.part * 8 + hn;
+      if (hn < nh) {
+        for (int d = dq; d < D; d += 4) p.part_o[pidx * D + d] = pend_o[hn * D + d];
+        if (dq == 0) p.part_lse[pidx] = pend_lse[hn];
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) *pend_flag = 0;            // the slot has been read
+      const int r = (it.b * p.Hkv + it.kvh) * p.HG + it.hg;
+      __threadfence();
+      int done = 0;
+      if (lane == 0) done = atomicAdd(&p.counters[r], 1) == it.nlive - 1;
+      done = __shfl_sync(0xffffffffu, done, 0);
+      if (done) {
+        __threadfence();
+        merge_row<D, T>(p, it, r, hn, dq, nh);
+        __syncwarp();
+        if (lane == 0) p.counters[r] = 0;
+      }
+    }
+    return;
+  }
 
   if (warp == kConsumers) {
     // ======================= producer warp =======================
@@ -221,7 +499,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     // other half of a double buffer while the current item's stages are issued,
     // so no stage waits on a dependent global load.
     uint32_t stage = 0;
-    auto prefetch_bt = [&](const Item& it, int buf) {
+    auto prefetch_bt = [&](const Piece& it, int buf) {
       const int32_t* row = p.block_table + (size_t)it.b * p.max_pages;
       const int first = it.t0 / p.P;
       const int n = (it.t1 - 1) / p.P - first + 1;
@@ -230,16 +508,15 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       cp_async_commit();
     };
     int buf = 0;
-    Item it{};
-    if ((int)blockIdx.x < total_items) {
-      it = decode_item(blockIdx.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
-      prefetch_bt(it, 0);
-    }
-    for (int i = blockIdx.x; i < total_items; i += gridDim.x, buf ^= 1) {
-      Item nx{};
-      const bool has_next = i + (int)gridDim.x < total_items;
+    Walker walk;
+    walk.init(p, prefix, lens);
+    Piece it{};
+    bool has = walk.next(it);
+    if (has) prefetch_bt(it, 0);
+    for (; has; buf ^= 1) {
+      Piece nx{};
+      const bool has_next = walk.next(nx);
       if (has_next) {
-        nx = decode_item(i + gridDim.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
         prefetch_bt(nx, buf ^ 1);
         cp_async_wait<1>();      // this item's slice has landed (the next may be in flight)
       } else {
@@ -296,6 +573,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       }
       __syncwarp();   // all lanes done with this buffer before it is refilled
       it = nx;
+      has = has_next;
     }
     // Drain: wait (bounded) for the last load issued into every slot.
     if (lane == 0) {
@@ -313,12 +591,13 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   const int c = lane & 3;    // fragment column pair
   const T* qbase = reinterpret_cast<const T*>(p.q);
   uint32_t stage = 0;
+
   // Q^T as the B operand (k = head_dim, n = head): b0b1 = q[n][16kc+2c..], b2b3 = +8.
   // The next item's fragments are loaded while the current item runs.
   // With FUSE the cos/sin pairs of the fragment's first-half columns at the new
   // token's position come along; the rotation happens when the item starts.
   constexpr int KH = KC / 2;            // k-chunks in the first half of head_dim
-  auto load_q = [&](const Item& it, uint32_t (&dst)[KC][2], uint32_t (&cs)[KH][2],
+  auto load_q = [&](const Piece& it, uint32_t (&dst)[KC][2], uint32_t (&cs)[KH][2],
                     uint32_t (&sn)[KH][2]) {
     const int ghead = it.hg * 8 + g;
     const bool ok = ghead < p.G;
@@ -343,21 +622,26 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   };
   uint32_t qf_next[KC][2];
   uint32_t cs_next[KH][2], sn_next[KH][2];
-  Item it_next{};
-  if ((int)blockIdx.x < total_items) {
-    it_next = decode_item(blockIdx.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
-    load_q(it_next, qf_next, cs_next, sn_next);
-  }
-  int item_seq = 0;   // items this CTA has finished
-  for (int i = blockIdx.x; i < total_items; i += gridDim.x) {
-    const Item it = it_next;
-    uint32_t qf[KC][2];
+  Walker walk;
+  walk.init(p, prefix, lens);
+  Piece it_next{};
+  bool has = walk.next(it_next);
+  if (has) load_q(it_next, qf_next, cs_next, sn_next);
+  int item_seq = 0;   // segments this CTA has finished
+  uint32_t qf[KC][2];
+  float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
+  float l_run[2] = {0.f, 0.f};               // per-thread partial sums
+  float o[KC][4];                            // O^T fragments: rows d, cols heads
+  while (has) {
+    const Piece it = it_next;
+    if (it.first) {
 #pragma unroll
-    for (int kc = 0; kc < KC; ++kc) {
-      qf[kc][0] = qf_next[kc][0];
-      qf[kc][1] = qf_next[kc][1];
+      for (int kc = 0; kc < KC; ++kc) {
+        qf[kc][0] = qf_next[kc][0];
+        qf[kc][1] = qf_next[kc][1];
+      }
     }
-    if constexpr (FUSE) {
+    if (FUSE && it.first) {
       // RoPE of the new token's query, in registers: element d of the first half
       // (chunk kc) pairs with d + D/2 (chunk kc + KC/2) held by the same lane.
 #pragma unroll
@@ -366,7 +650,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         for (int r = 0; r < 2; ++r) rope_pair2<T>(qf[kc][r], qf[kc + KH][r], cs_next[kc][r], sn_next[kc][r]);
       // The partition-0 item of each head group publishes the rotated query.
       const int ghead = it.hg * 8 + g;
-      if (p.q_rot_out != nullptr && it.part == 0 && warp == 0 && ghead < p.G) {
+      if (p.q_rot_out != nullptr && it.t0 == 0 && warp == 0 && ghead < p.G) {
         uint32_t* qo = reinterpret_cast<uint32_t*>(
             reinterpret_cast<T*>(p.q_rot_out) + ((size_t)it.b * p.Hq + it.kvh * p.G + ghead) * D);
 #pragma unroll
@@ -376,16 +660,15 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
       }
     }
-    if (i + (int)gridDim.x < total_items) {
-      it_next = decode_item(i + gridDim.x, prefix, p.B, p.Hkv, p.HG, lens, p.T);
-      load_q(it_next, qf_next, cs_next, sn_next);
-    }
+    has = walk.next(it_next);
+    if (has && it_next.first) load_q(it_next, qf_next, cs_next, sn_next);
     const int nstage = (it.t1 - it.t0 + ST - 1) / ST;
-    float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
-    float l_run[2] = {0.f, 0.f};               // per-thread partial sums
-    float o[KC][4];                            // O^T fragments: rows d, cols heads
+    if (it.first) {
+      m_run[0] = m_run[1] = -INFINITY;
+      l_run[0] = l_run[1] = 0.f;
 #pragma unroll
-    for (int mt = 0; mt < KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+      for (int mt = 0; mt < KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    }
 
     constexpr int NT = ST / 16;                 // 16-token tiles per stage
     constexpr int NTL = NT / kWarpsPerGroup;    // tiles of this warp
@@ -550,7 +833,9 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       if (lane == 0) mbar_arrive(smem_u32(&empty_bar[slot]));
     }
 
-    // ---- item epilogue: combine the consumer warps ----
+    if (!it.last) continue;   // the segment goes on in the next piece
+
+    // ---- segment epilogue: combine the consumer warps ----
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       l_run[j] += __shfl_xor_sync(0xffffffffu, l_run[j], 4);
@@ -594,7 +879,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     if (last) {
       __threadfence_block();
       const int nh = min(8, p.G - it.hg * 8);
-      const bool single = it.L <= p.T;  // the sequence has one partition
+      const bool single = it.whole;     // no other CTA or partition shares the row
       // Per-head weights once: lane n < 8 owns head n.  Warps without tokens have
       // m = -inf and weight 0.
       float wsc[kConsumers];
@@ -610,9 +895,32 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       const float inv = single ? 1.f / fmaxf(lsum, 1e-9f) : 1.f / lsum;
       // Lane = (head hn, quarter of head_dim): 8 heads x 4 lanes.
       const int dq = lane >> 3;
-      if (hn < nh) {
+      const bool handoff = p.balanced && !single;
+      if (handoff) {
+        // Wait (bounded) until the merge warp has taken the previous segment.
+        const unsigned long long t0 = globaltimer_ns();
+        while (*pend_flag != 0 && !*abort_flag) {
+          if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+            *abort_flag = 1;
+            atomicOr(p.status, kStatusWaitTimeout);
+          }
+        }
+        __threadfence_block();
+      }
+      if (handoff && hn < nh) {
+        for (int d = dq; d < D; d += 4) {
+          float acc = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumers; ++w) acc += comb_o[(w * D + d) * 8 + hn] * wsc[w];
+          pend_o[hn * D + d] = acc * inv;
+        }
+        if (dq == 0) pend_lse[hn] = M + log2f(lsum);
+      } else if (hn < nh) {
         const int hq = it.kvh * p.G + it.hg * 8 + hn;
         const size_t row = (size_t)it.b * p.Hq + hq;
+        // Partial index: uniform [B, Hq, max_parts]; balanced [slot][8 heads].
+        const size_t pidx = p.balanced ? (size_t)it.part * 8 + hn
+                                       : row * p.max_parts + it.part;
         for (int d = dq; d < D; d += 4) {
           float acc = 0.f;
 #pragma unroll
@@ -620,10 +928,15 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
           if (single) {
             reinterpret_cast<T*>(p.out)[row * D + d] = from_f32<T>(acc * inv);
           } else {
-            p.part_o[(row * p.max_parts + it.part) * D + d] = acc * inv;
+            p.part_o[(pidx * D) + d] = acc * inv;
           }
         }
-        if (!single && dq == 0) p.part_lse[row * p.max_parts + it.part] = M + log2f(lsum);
+        if (!single && dq == 0) p.part_lse[pidx] = M + log2f(lsum);
+      }
+      if (handoff) {
+        __threadfence_block();
+        __syncwarp();
+        if (lane == 0) *pend_flag = 1;   // the merge warp publishes it, merges when complete
       }
       __syncwarp();
       if (lane == 0) {
@@ -908,10 +1221,11 @@ static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const v
     return cudaErrorInvalidValue;
   const DeviceInfo di = device_info();
   constexpr int STAGE_BYTES = 2 * (D / 64) * ST * fast::kRowBytes;
-  p.max_entries = p.T / p.P + 2;
+  p.max_entries = (p.balanced ? p.cap_chunks * fast::kStageTok : p.T) / p.P + 2;
   const size_t fixed = 1024 /*align*/ + sizeof(float) * (fast::kConsumers * D * 8 + 16 * fast::kConsumers) +
                        2 * fast::kMaxStages * sizeof(uint64_t) +
-                       sizeof(int) * (2 * p.B + 4 + 2 * p.max_entries) + 64;
+                       sizeof(int) * (2 * p.B + 4 + 2 * p.max_entries) + 64 +
+                       sizeof(int) * 32 + sizeof(float) * (8 * D + 8);   // handoff slot
   const size_t budget = (size_t)di.max_smem_optin;
   int nst = (int)((budget - fixed) / STAGE_BYTES);
   if (nst > fast::kMaxStages) nst = fast::kMaxStages;
@@ -925,9 +1239,11 @@ static cudaError_t launch_fast_t(const fast::Params& p0, const void* kp, const v
   auto kern = fast::paged_decode_tma_kernel<D, T, ST, FUSE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  long long upper = (long long)p.B * p.max_parts * p.Hkv * p.HG;
   int grid = di.sms;
-  if (upper < grid) grid = (int)(upper > 0 ? upper : 1);
+  if (!p.balanced) {
+    const long long upper = (long long)p.B * p.max_parts * p.Hkv * p.HG;
+    if (upper < grid) grid = (int)(upper > 0 ? upper : 1);
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -949,6 +1265,33 @@ static cudaError_t launch_lse_merge_ex(const float* part_o, const float* part_ls
                                        cudaStream_t stream, const int32_t* lens_next,
                                        int32_t* seq_lens_out);
 
+// Pieces of the balanced split are at most this many 64-token chunks (the block-table
+// slice of one piece is staged in shared memory).
+constexpr int kBalancedCapChunks = 32;
+
+int balanced_grid() { return device_info().sms; }
+
+// Work split of the fast kernel: uniform partitions of Tpart tokens, or (Tpart == 0)
+// the balanced split, whose counters head the part_lse buffer.
+static void set_split(fast::Params& p, int Tpart, float* part_o, float* part_lse) {
+  p.part_o = part_o;
+  if (Tpart == 0) {
+    p.balanced = 1;
+    p.cap_chunks = kBalancedCapChunks;
+    p.counters = reinterpret_cast<int32_t*>(part_lse);
+    p.part_lse = part_lse + balanced_counter_words(p.B * p.Hkv * p.HG);
+    p.T = 0;
+    p.max_parts = 0;
+  } else {
+    p.balanced = 0;
+    p.cap_chunks = 0;
+    p.counters = nullptr;
+    p.part_lse = part_lse;
+    p.T = Tpart;
+    p.max_parts = (p.max_pages * p.P + Tpart - 1) / Tpart;
+  }
+}
+
 template <bool FUSE>
 static cudaError_t launch_fast(const fast::Params& p, int dtype, int D, const void* kp,
                                const void* vp, std::string* err, cudaStream_t stream) {
@@ -956,11 +1299,11 @@ static cudaError_t launch_fast(const fast::Params& p, int dtype, int D, const vo
   if (dtype == LLMC_BF16) {
     if (D == 64) return launch_fast_t<64, __nv_bfloat16, 64, FUSE>(p, kp, vp, nrows, err, stream);
     if (D == 128) return launch_fast_t<128, __nv_bfloat16, 64, FUSE>(p, kp, vp, nrows, err, stream);
-    return launch_fast_t<256, __nv_bfloat16, 64, FUSE>(p, kp, vp, nrows, err, stream);
+    return launch_fast_t<256, __nv_bfloat16, 32, FUSE>(p, kp, vp, nrows, err, stream);
   }
   if (D == 64) return launch_fast_t<64, __half, 64, FUSE>(p, kp, vp, nrows, err, stream);
   if (D == 128) return launch_fast_t<128, __half, 64, FUSE>(p, kp, vp, nrows, err, stream);
-  return launch_fast_t<256, __half, 64, FUSE>(p, kp, vp, nrows, err, stream);
+  return launch_fast_t<256, __half, 32, FUSE>(p, kp, vp, nrows, err, stream);
 }
 
 // Fused RoPE + page append + decode + merge (one decode launch, one merge launch).
@@ -977,20 +1320,22 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
   if (!fast_path_applies(dtype, D, P, max_pages, Tpart, B, q_raw, kp, vp))
     return cudaErrorNotSupported;
   const int G = Hq / Hkv;
-  const int max_parts = (max_pages * P + Tpart - 1) / Tpart;
   fast::Params p;
-  p.q = q_raw; p.out = out; p.part_o = part_o; p.part_lse = part_lse; p.block_table = bt;
+  p.q = q_raw; p.out = out; p.block_table = bt;
   p.seq_lens = seq_lens; p.status = status;
   p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
-  p.max_pages = max_pages; p.T = Tpart; p.max_parts = max_parts; p.num_pages = num_pages;
+  p.max_pages = max_pages; p.num_pages = num_pages;
+  set_split(p, Tpart, part_o, part_lse);
   p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
   p.k_new = k_new; p.v_new = v_new; p.cos_tab = cos_tab; p.sin_tab = sin_tab;
   p.k_pages = kp; p.v_pages = vp; p.q_rot_out = q_rot_out; p.lens_next = lens_next;
   p.rope_max_pos = rope_max_pos;
+  p.seq_lens_out = seq_lens;
   cudaError_t e = launch_fast<true>(p, dtype, D, kp, vp, err, stream);
   if (e != cudaSuccess) return e;
-  return launch_lse_merge_ex(part_o, part_lse, seq_lens, out, B, Hq, D, max_parts, Tpart,
-                             max_parts * Tpart, dtype, stream, lens_next, seq_lens);
+  if (p.balanced) return cudaSuccess;   // merged and published inside the decode kernel
+  return launch_lse_merge_ex(part_o, part_lse, seq_lens, out, B, Hq, D, p.max_parts, Tpart,
+                             p.max_parts * Tpart, dtype, stream, lens_next, seq_lens);
 }
 
 cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, const int32_t* bt,
@@ -999,20 +1344,27 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
                                 int P, int max_pages, int num_pages, int Tpart, float scale,
                                 int dtype, int flags, std::string* err, cudaStream_t stream) {
   const int G = Hq / Hkv;
-  const int max_parts = (max_pages * P + Tpart - 1) / Tpart;
   if (B == 0) return cudaSuccess;
-  if (!(flags & LLMC_DECODE_FORCE_GENERIC) &&
-      fast_path_applies(dtype, D, P, max_pages, Tpart, B, q, kp, vp)) {
+  const bool fast_ok = !(flags & LLMC_DECODE_FORCE_GENERIC) &&
+                       fast_path_applies(dtype, D, P, max_pages, Tpart, B, q, kp, vp);
+  if (Tpart == 0 && !fast_ok) {
+    *err = "the balanced split (partition_tokens 0) needs the TMA kernel's shapes";
+    return cudaErrorNotSupported;
+  }
+  const int max_parts = Tpart > 0 ? (max_pages * P + Tpart - 1) / Tpart : 0;
+  if (fast_ok) {
     fast::Params p;
-    p.q = q; p.out = out; p.part_o = part_o; p.part_lse = part_lse; p.block_table = bt;
+    p.q = q; p.out = out; p.block_table = bt;
     p.seq_lens = seq_lens; p.status = status;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
-    p.max_pages = max_pages; p.T = Tpart; p.max_parts = max_parts; p.num_pages = num_pages;
+    p.max_pages = max_pages; p.num_pages = num_pages;
+    set_split(p, Tpart, part_o, part_lse);
     p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
     p.k_new = p.v_new = p.cos_tab = p.sin_tab = nullptr;
     p.k_pages = p.v_pages = p.q_rot_out = nullptr;
     p.lens_next = nullptr;
     p.rope_max_pos = 0;
+    p.seq_lens_out = nullptr;
     return launch_fast<false>(p, dtype, D, kp, vp, err, stream);
   }
   // generic SIMT path
@@ -1051,6 +1403,7 @@ static cudaError_t launch_lse_merge_ex(const float* part_o, const float* part_ls
 cudaError_t launch_lse_merge(const float* part_o, const float* part_lse, const int32_t* seq_lens,
                              void* out, int B, int Hq, int D, int max_parts, int Tpart, int cap,
                              int dtype, cudaStream_t stream) {
+  if (Tpart == 0) return cudaSuccess;   // the balanced decode kernel merges its own rows
   return launch_lse_merge_ex(part_o, part_lse, seq_lens, out, B, Hq, D, max_parts, Tpart, cap,
                              dtype, stream, nullptr, nullptr);
 }

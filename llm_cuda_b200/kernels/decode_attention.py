@@ -32,6 +32,10 @@ from .. import _native as N
 _ATTN_EPSILON: float = 1e-9
 _MAX_BLOCK_D: int = 256
 
+# partition_tokens value of the balanced split (LLMC_PARTITION_BALANCED): every SM
+# takes an equal share of all rows' 64-token chunks, computed on the device.
+BALANCED = 0
+
 _PARTITION_CANDIDATES = (256, 512, 1024, 2048, 4096, 8192)
 # Fixed cost of a work item in token-equivalents (pipeline fill + epilogue).
 _ITEM_OVERHEAD_TOKENS = 96
@@ -109,6 +113,7 @@ class DecodeWorkspace:
         self.device = device
         self.part_o = torch.empty(0, dtype=torch.float32, device=device)
         self.part_lse = torch.empty(0, dtype=torch.float32, device=device)
+        self._counter_words = None
 
     def lens_next(self, B: int) -> torch.Tensor:
         """int32 [B] scratch for the fused step's advanced lengths."""
@@ -116,9 +121,40 @@ class DecodeWorkspace:
             self._lens_next = torch.empty(B, dtype=torch.int32, device=self.device)
         return self._lens_next
 
+    def get_balanced(self, B: int, Hq: int, Hkv: int, d: int):
+        """Partials of the balanced split (``partition_tokens = 0``); sizes from
+        ``llmc_balanced_partials_bytes`` on this device.
+
+        ``part_lse`` starts with the kernel's per-row counters, which must be zero
+        before a call; the kernel returns them to zero.  They are zeroed here when the
+        buffer is new or the row count (hence the counter area) changes.
+        """
+        lib = N.load()
+        lse_b = N.ctypes.c_size_t(0)
+        with torch.cuda.device(self.device):
+            o_b = lib.llmc_balanced_partials_bytes(B, Hq, Hkv, d, N.ctypes.byref(lse_b))
+        no, nl = o_b // 4, lse_b.value // 4
+        if self.part_o.numel() < no:
+            self.part_o = torch.empty(no, dtype=torch.float32, device=self.device)
+        if self.part_lse.numel() < nl:
+            self.part_lse = torch.zeros(nl, dtype=torch.float32, device=self.device)
+            self._counter_words = None
+        rows = B * Hkv * ((Hq // Hkv + 7) // 8)
+        words = ((rows + 1) + 31) // 32 * 32
+        if self._counter_words != words:
+            self.part_lse[:words].zero_()
+            self._counter_words = words
+        return self.part_o, self.part_lse
+
+    def invalidate_counters(self) -> None:
+        """Re-zero the balanced split's counters on next use (after a kernel gave up
+        mid-step, e.g. on a wait timeout, they may be left counting)."""
+        self._counter_words = None
+
     def get(self, B: int, Hq: int, d: int, max_parts: int):
         if max_parts <= 1:
             return None, None
+        self._counter_words = None   # uniform partials overwrite the balanced counters
         no = B * Hq * max_parts * d
         nl = B * Hq * max_parts
         if self.part_o.numel() < no:
@@ -187,20 +223,29 @@ def paged_decode(
     if Hq % Hkv:
         raise ValueError("n_heads must be a multiple of n_kv_heads")
     max_pages = block_table.shape[1]
+    dt = N.dtype_code(q.dtype)
     if partition_tokens is None:
-        lens = host_lens if host_lens is not None else [max_pages * P] * B
-        partition_tokens = choose_partition_tokens(lens, Hkv, Hq // Hkv, _num_sms(q.device),
-                                                   max_tokens=max_pages * P)
+        if force_generic or not lib.llmc_decode_balanced_supported(
+                q3.data_ptr(), key_pages.data_ptr(), value_pages.data_ptr(), dt, d, P,
+                max_pages, B):
+            lens = host_lens if host_lens is not None else [max_pages * P] * B
+            partition_tokens = choose_partition_tokens(
+                lens, Hkv, Hq // Hkv, _num_sms(q.device), max_tokens=max_pages * P)
+        else:
+            partition_tokens = BALANCED
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     if out is None:
         out = torch.empty_like(q3)
     ws = workspace if workspace is not None else _default_workspace(q.device)
-    max_parts = -(-(max_pages * P) // partition_tokens)   # llmc_num_partitions
-    part_o, part_lse = ws.get(B, Hq, d, max_parts)
+    if partition_tokens == BALANCED:
+        max_parts = 0
+        part_o, part_lse = ws.get_balanced(B, Hq, Hkv, d)
+    else:
+        max_parts = -(-(max_pages * P) // partition_tokens)   # llmc_num_partitions
+        part_o, part_lse = ws.get(B, Hq, d, max_parts)
     st = status if status is not None else default_status(q.device)
     stream = N.stream_handle(q.device)
-    dt = N.dtype_code(q.dtype)
     if events is not None:
         events[0].record()
     rc = lib.llmc_paged_decode(
@@ -263,16 +308,16 @@ def rope_append_decode(
     v = v.contiguous()
     max_pages = block_table.shape[1]
     if partition_tokens is None:
-        lens = [x + 1 for x in host_lens] if host_lens is not None else [max_pages * P] * B
-        partition_tokens = choose_partition_tokens(lens, Hkv, Hq // Hkv, _num_sms(q.device),
-                                                   max_tokens=max_pages * P)
+        partition_tokens = BALANCED
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     out = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device) if out is None else out
     q_out = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device) if q_out is None else q_out
     ws = workspace if workspace is not None else _default_workspace(q.device)
-    max_parts = -(-(max_pages * P) // partition_tokens)
-    part_o, part_lse = ws.get(B, Hq, d, max_parts)
+    if partition_tokens == BALANCED:
+        part_o, part_lse = ws.get_balanced(B, Hq, Hkv, d)
+    else:
+        part_o, part_lse = ws.get(B, Hq, d, -(-(max_pages * P) // partition_tokens))
     st = status if status is not None else default_status(q.device)
     if events is not None:
         events[0].record()

@@ -203,7 +203,11 @@ class PagedKVLayerCache:
 
     def check_status(self) -> None:
         """Synchronise and raise ``DeviceStatusError`` if a kernel flagged an error."""
-        N.raise_on_status(self.status)
+        try:
+            N.raise_on_status(self.status)
+        except N.DeviceStatusError:
+            self.workspace.invalidate_counters()
+            raise
 
 
 class PagedKVCache:
@@ -257,21 +261,19 @@ class GraphedDecodeStep:
     refills before each ``replay()``; the step rotates, appends at ``seq_lens`` and
     attends, advancing the lengths on the device and in ``cache.host_lengths``.  One
     graph launch per step instead of several Python-issued launches: the host cost of
-    a step is that of ``cudaGraphLaunch``.  ``partition_tokens`` is fixed at capture.
+    a step is that of ``cudaGraphLaunch``.  By default the step uses the balanced
+    split, which the kernel recomputes from the device lengths at every replay, so
+    the work stays even across SMs as the contexts grow.
     """
 
     def __init__(self, cache: PagedKVLayerCache, rope: RopeTable, q: torch.Tensor,
                  k: torch.Tensor, v: torch.Tensor, partition_tokens: int | None = None,
                  out: torch.Tensor | None = None):
-        from ...kernels.decode_attention import choose_partition_tokens, _num_sms
+        from ...kernels.decode_attention import BALANCED
 
         self.cache, self.rope, self.q, self.k, self.v = cache, rope, q, k, v
         B, Hq, d = q.shape[0], q.shape[1], q.shape[-1]
-        if partition_tokens is None:
-            partition_tokens = choose_partition_tokens(
-                [x + 1 for x in cache.host_lengths], cache.num_kv_heads, Hq // cache.num_kv_heads,
-                _num_sms(q.device), max_tokens=cache.max_pages * cache.page_size)
-        self.partition_tokens = partition_tokens
+        self.partition_tokens = BALANCED if partition_tokens is None else partition_tokens
         self.out = out if out is not None else torch.empty(B, Hq, d, dtype=q.dtype,
                                                            device=q.device)
         self.q_rot = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device)

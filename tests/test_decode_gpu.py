@@ -252,6 +252,66 @@ def test_empty_and_short_contexts(force_generic):
     _check_samples(cache, q, out, list(range(1, len(lens))), "short")
 
 
+# ---------------------------------------------------------------------------
+# Balanced split (partition_tokens = 0): equal chunk ranges per CTA
+# ---------------------------------------------------------------------------
+BALANCED_CASES = {
+    # name: (B, Hq, Hkv, d, lens, page, dtype)
+    "fewer_chunks_than_ctas": (1, 8, 8, 128, [100], 16, torch.bfloat16),
+    "two_head_groups": (3, 64, 4, 128, [5000, 0, 3000], 16, torch.bfloat16),
+    "d64_page8_ragged": (5, 32, 8, 64, [1, 64, 65, 7000, 129], 8, torch.bfloat16),
+    "d256_page32": (2, 16, 2, 256, [20000, 333], 32, torch.bfloat16),
+    "page128_fp16": (7, 32, 8, 128, [128, 4096, 17, 9000, 1, 2048, 3333], 128, torch.float16),
+    "one_row_many_ctas": (1, 4, 1, 128, [131072], 64, torch.bfloat16),
+}
+
+
+@pytest.mark.parametrize("name", list(BALANCED_CASES))
+def test_balanced_split_matches_oracle(name):
+    B, Hq, Hkv, d, lens, P, dtype = BALANCED_CASES[name]
+    cache, q = _random_paged(B, Hq, Hkv, d, [max(L, 1) for L in lens], P, dtype, 2100)
+    cache.seq_lens.copy_(torch.tensor(lens, dtype=torch.int32))
+    cache.host_lengths = list(lens)
+    lib = N.load()
+    assert lib.llmc_decode_balanced_supported(q.data_ptr(), cache.key_pages.data_ptr(),
+                                              cache.value_pages.data_ptr(),
+                                              N.dtype_code(dtype), d, P, cache.max_pages, B)
+    out = paged_decode(q, cache.key_pages, cache.value_pages, cache.block_table, cache.seq_lens,
+                       partition_tokens=0, status=cache.status, workspace=cache.workspace)
+    cache.check_status()
+    # the in-kernel merge leaves its counters at zero, so a second call is identical
+    rows = B * Hkv * ((Hq // Hkv + 7) // 8)
+    words = ((rows + 1) + 31) // 32 * 32
+    counters = cache.workspace.part_lse[:words].view(torch.int32)
+    assert torch.count_nonzero(counters) == 0
+    again = paged_decode(q, cache.key_pages, cache.value_pages, cache.block_table,
+                         cache.seq_lens, partition_tokens=0, status=cache.status,
+                         workspace=cache.workspace)
+    assert torch.equal(again, out)
+    for b, L in enumerate(lens):
+        if L == 0:
+            assert torch.count_nonzero(out[b]) == 0
+    live = [b for b, L in enumerate(lens) if L > 0]
+    _check_samples(cache, q, out, live, f"balanced/{name}")
+    # the same rows through the SIMT kernel with uniform partitions
+    gen = paged_decode(q, cache.key_pages, cache.value_pages, cache.block_table, cache.seq_lens,
+                       partition_tokens=1024, force_generic=True, status=cache.status)
+    assert (out.float() - gen.float()).abs().max().item() < 2e-2
+
+
+def test_balanced_split_rejects_simt_only_shapes():
+    """fp32 has no TMA kernel: the explicit balanced split is refused, not emulated."""
+    cache, q = _random_paged(2, 8, 2, 128, [300, 40], 16, torch.float32, 2101)
+    with pytest.raises(N.NativeLibraryError, match="balanced"):
+        paged_decode(q, cache.key_pages, cache.value_pages, cache.block_table, cache.seq_lens,
+                     partition_tokens=0, status=cache.status)
+    # the default picks uniform partitions for this shape
+    out = paged_decode(q, cache.key_pages, cache.value_pages, cache.block_table, cache.seq_lens,
+                       host_lens=[300, 40], status=cache.status)
+    cache.check_status()
+    _check_samples(cache, q, out, [0, 1], "fp32 default")
+
+
 def test_bad_page_is_reported_not_faulted():
     cache, q = _random_paged(2, 8, 2, 128, [100, 100], 16, torch.bfloat16, 2006)
     cache.block_table[1, 3] = cache.num_pages + 1000
@@ -448,3 +508,33 @@ def test_graphed_decode_step_matches_eager_two_steps():
         assert torch.equal(out.view_as(eager[i]), eager[i])
     cache.check_status()
     assert cache.seq_lens.tolist() == [L + 2 for L in lens] and cache.host_lengths == [L + 2 for L in lens]
+
+
+def test_fused_balanced_steps_match_uniform_partitions():
+    """Six fused steps with the balanced split (in-kernel merge, lengths published by
+    the decode launch) against the same steps with uniform 128-token partitions;
+    contexts cross 64-token chunk edges and include an empty one."""
+    B, Hq, Hkv, d, P = 6, 32, 8, 128, 16
+    lens = [0, 62, 63, 64, 1000, 4093]
+    cache, _ = _random_paged(B, Hq, Hkv, d, [L + 8 for L in lens], P, torch.bfloat16, 2013)
+    rope = RopeTable(cache.max_seq_len, d, C.THETA, DEV, torch.bfloat16)
+    gd = torch.Generator(device=DEV).manual_seed(13)
+    kp0, vp0 = cache.key_pages.clone(), cache.value_pages.clone()
+    steps = [tuple(torch.randn(B, h, 1, d, device=DEV, generator=gd).bfloat16()
+                   for h in (Hq, Hkv, Hkv)) for _ in range(6)]
+
+    def run(T):
+        cache.key_pages.copy_(kp0)
+        cache.value_pages.copy_(vp0)
+        cache.seq_lens.copy_(torch.tensor(lens, dtype=torch.int32))
+        cache.host_lengths = list(lens)
+        outs = [cache.rope_append_decode(q, k, v, rope, partition_tokens=T).clone()
+                for q, k, v in steps]
+        cache.check_status()
+        assert cache.seq_lens.tolist() == [L + 6 for L in lens]
+        return torch.stack(outs)
+
+    bal = run(0)
+    uni = run(128)
+    assert (bal.float() - uni.float()).abs().max().item() < 2e-2
+    assert torch.isfinite(bal.float()).all()
