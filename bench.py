@@ -207,7 +207,7 @@ def run_reference(args, w, lengths):
         "impl": "reference", "metric": "decode-attn KV GB/s", "value": value, "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": el / args.steps * 1e3 * (full_kv / (units * L * d * 4)),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": w["scaling"], "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": {"workload": w["desc"], "sample_units_per_step": units},
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
                          "sample": f"{units} (sequence, KV head) units of ctx {L} per step "
@@ -534,11 +534,12 @@ def run_ours(args, name, w, lengths):
         line = {
             "metric": "decode-attn KV GB/s", "value": value, "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": w["scaling"], "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic (seeded N(0,1) K/V pages, q/k/v of the new token)",
             "tokens_per_s": tokens_s,
             "hbm_frac_step": value / world / peaks["hbm_gbs"],
-            "config": {"workload": w["desc"], "B": B, "Hq": Hq, "Hkv": Hkv, "head_dim": d,
+            "config": {"workload": w["desc"], "B": B, "global_batch": B, "Hq": Hq, "Hkv": Hkv,
+                       "head_dim": d,
                        "page_size": P, "context_tokens_total": sum(lengths),
                        "partition_tokens": T if T else "balanced",
                        "parallelism": f"tp{world} (KV-head sharded)",
@@ -703,6 +704,9 @@ def main():
                     help="also time the reference's Triton decode kernel (baseline/_ref)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of oracle CPU-baseline sampling at N=1 (0: skip)")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
+                    help="N>1: weak = N x the config's batch, head-sharded (per-GPU work "
+                         "fixed); strong = the config's batch split over N GPUs")
     args = ap.parse_args()
     if args.workload == "c5":
         if args.impl == "reference":
@@ -711,7 +715,14 @@ def main():
             return
         run_c5(args)
         return
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    w["scaling"] = args.scaling
+    if args.scaling == "weak" and world > 1:
+        # Weak scaling: the config's batch per GPU, N times the sequences in all,
+        # every rank holding its 1/N of the KV heads of all of them.
+        w["B"] *= world
+        w["desc"] += f" (global batch {w['B']} = {world} x the config's, weak scaling)"
     lengths = _lengths(args.workload, w)
     if args.impl == "reference":
         run_reference(args, w, lengths)

@@ -620,6 +620,49 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
     }
   };
+  constexpr int NT = ST / 16;                 // 16-token tiles per stage
+  constexpr int NTL = NT / kWarpsPerGroup;    // tiles of this warp
+  const int sub = warp % kWarpsPerGroup;
+  // FUSE: the new token's raw k/v, cos/sin and page id, fetched one piece ahead by
+  // the warp whose tile will hold the token, so that patching it into the landed
+  // tile costs no global round trip on the streaming path.  Lane j holds elements
+  // i = 2j + 64n of each half of head_dim.
+  constexpr int NI = (D / 2 + 63) / 64;
+  struct NewTok {
+    uint32_t k1[NI], k2[NI], v1[NI], v2[NI], cs[NI], sn[NI];
+    int page;
+  };
+  auto fetch_newtok = [&](const Piece& x, NewTok& nt) {
+    const int pos = x.L - 1;
+    const T* kn = reinterpret_cast<const T*>(p.k_new) + ((size_t)x.b * p.Hkv + x.kvh) * D;
+    const T* vn = reinterpret_cast<const T*>(p.v_new) + ((size_t)x.b * p.Hkv + x.kvh) * D;
+    const T* crow = reinterpret_cast<const T*>(p.cos_tab) + (size_t)pos * D;
+    const T* srow = reinterpret_cast<const T*>(p.sin_tab) + (size_t)pos * D;
+    nt.page = __ldg(p.block_table + (size_t)x.b * p.max_pages + pos / p.P);
+#pragma unroll
+    for (int n = 0; n < NI; ++n) {
+      const int i = 2 * lane + 64 * n;
+      if (i < D / 2) {
+        nt.k1[n] = __ldg(reinterpret_cast<const uint32_t*>(kn + i));
+        nt.k2[n] = __ldg(reinterpret_cast<const uint32_t*>(kn + i + D / 2));
+        nt.v1[n] = __ldg(reinterpret_cast<const uint32_t*>(vn + i));
+        nt.v2[n] = __ldg(reinterpret_cast<const uint32_t*>(vn + i + D / 2));
+        nt.cs[n] = __ldg(reinterpret_cast<const uint32_t*>(crow + i));
+        nt.sn[n] = __ldg(reinterpret_cast<const uint32_t*>(srow + i));
+      }
+    }
+  };
+  // Does this warp patch the new token of piece x, whose first stage is stage0?
+  auto owns_newtok = [&](const Piece& x, uint32_t stage0) -> bool {
+    const int pos = x.L - 1;
+    if (!FUSE || pos < x.t0 || pos >= x.t1) return false;
+    const int s_new = (pos - x.t0) / ST;
+    if ((int)((stage0 + s_new) % kGroups) != warp / kWarpsPerGroup) return false;
+    return (pos - x.t0 - s_new * ST) / (NTL * 16) == sub;
+  };
+  NewTok nt_next;
+  bool nt_next_ok = false;
+
   uint32_t qf_next[KC][2];
   uint32_t cs_next[KH][2], sn_next[KH][2];
   Walker walk;
@@ -627,6 +670,10 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   Piece it_next{};
   bool has = walk.next(it_next);
   if (has) load_q(it_next, qf_next, cs_next, sn_next);
+  if (has && owns_newtok(it_next, 0)) {
+    fetch_newtok(it_next, nt_next);
+    nt_next_ok = true;
+  }
   int item_seq = 0;   // segments this CTA has finished
   uint32_t qf[KC][2];
   float m_run[2] = {-INFINITY, -INFINITY};   // heads 2c, 2c+1 (log2 domain)
@@ -660,9 +707,16 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         }
       }
     }
+    NewTok nt = nt_next;
+    bool nt_ok = nt_next_ok;
+    const int nstage = (it.t1 - it.t0 + ST - 1) / ST;
     has = walk.next(it_next);
     if (has && it_next.first) load_q(it_next, qf_next, cs_next, sn_next);
-    const int nstage = (it.t1 - it.t0 + ST - 1) / ST;
+    nt_next_ok = false;
+    if (has && owns_newtok(it_next, stage + nstage)) {
+      fetch_newtok(it_next, nt_next);
+      nt_next_ok = true;
+    }
     if (it.first) {
       m_run[0] = m_run[1] = -INFINITY;
       l_run[0] = l_run[1] = 0.f;
@@ -670,9 +724,6 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       for (int mt = 0; mt < KC; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     }
 
-    constexpr int NT = ST / 16;                 // 16-token tiles per stage
-    constexpr int NTL = NT / kWarpsPerGroup;    // tiles of this warp
-    const int sub = warp % kWarpsPerGroup;
     for (int s = 0; s < nstage; ++s, ++stage) {
       if ((int)(stage % kGroups) != warp / kWarpsPerGroup) continue;
       const int slot = stage % nst;
@@ -693,22 +744,21 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
         const int pos = it.L - 1;
         const int r = pos - tok0;
         if (r >= row_lo && r < row_lo + my_valid) {
-          const T* kn = reinterpret_cast<const T*>(p.k_new) + ((size_t)it.b * p.Hkv + it.kvh) * D;
-          const T* vn = reinterpret_cast<const T*>(p.v_new) + ((size_t)it.b * p.Hkv + it.kvh) * D;
-          const T* crow = reinterpret_cast<const T*>(p.cos_tab) + (size_t)pos * D;
-          const T* srow = reinterpret_cast<const T*>(p.sin_tab) + (size_t)pos * D;
-          const int page = p.block_table[(size_t)it.b * p.max_pages + pos / p.P];
+          if (!nt_ok) fetch_newtok(it, nt);   // not prefetched (not expected): fetch now
+          const int page = nt.page;
           const bool write_page = it.hg == 0 && page >= 0 && page < p.num_pages;
           T* kp = reinterpret_cast<T*>(p.k_pages) +
                   (((size_t)(write_page ? page : 0) * p.Hkv + it.kvh) * p.P + pos % p.P) * D;
           T* vp = reinterpret_cast<T*>(p.v_pages) + (kp - reinterpret_cast<T*>(p.k_pages));
-          for (int i = 2 * lane; i < D / 2; i += 64) {
-            uint32_t x1 = *reinterpret_cast<const uint32_t*>(kn + i);
-            uint32_t x2 = *reinterpret_cast<const uint32_t*>(kn + i + D / 2);
-            rope_pair2<T>(x1, x2, *reinterpret_cast<const uint32_t*>(crow + i),
-                          *reinterpret_cast<const uint32_t*>(srow + i));
-            const uint32_t v1 = *reinterpret_cast<const uint32_t*>(vn + i);
-            const uint32_t v2 = *reinterpret_cast<const uint32_t*>(vn + i + D / 2);
+#pragma unroll
+          for (int n = 0; n < NI; ++n) {
+            const int i = 2 * lane + 64 * n;
+            if (i >= D / 2) continue;
+            uint32_t x1 = nt.k1[n];
+            uint32_t x2 = nt.k2[n];
+            rope_pair2<T>(x1, x2, nt.cs[n], nt.sn[n]);
+            const uint32_t v1 = nt.v1[n];
+            const uint32_t v2 = nt.v2[n];
             *reinterpret_cast<uint32_t*>(kst + smem_off(r, i) + (i & 7) * 2) = x1;
             *reinterpret_cast<uint32_t*>(kst + smem_off(r, i + D / 2) + (i & 7) * 2) = x2;
             *reinterpret_cast<uint32_t*>(vst + smem_off(r, i) + (i & 7) * 2) = v1;
