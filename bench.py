@@ -550,7 +550,9 @@ def run_ours(args, name, w, lengths):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"],
                          "unit": "GB/s", "frac": achieved / peaks["hbm_gbs"],
                          "traffic": _profile_traffic(name, world),
-                         "kernel": "paged_decode_tma_kernel<128,bf16,64,fused> + lse_merge_kernel",
+                         "kernel": ("paged_decode_tma_kernel<128,bf16,64,fused> (balanced split, "
+                                    "in-kernel merge)") if T == BALANCED else
+                                   "paged_decode_tma_kernel<128,bf16,64,fused> + lse_merge_kernel",
                          "kernel_ms": k_ms, "algorithmic_bytes": alg,
                          "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"},
             "cpu_baseline": cpu,
@@ -561,7 +563,9 @@ def run_ours(args, name, w, lengths):
                     "path": "GraphedDecodeStep (the fused RoPE+append+decode step, one graph "
                             "launch per step) with pinned host in/out, copies on a second "
                             "stream overlapping compute"},
-            "gpu_launches": 3 * args.steps,
+            # per step: the fused decode launch (+ the merge launch with uniform
+            # partitions); the length reset is a graph memcpy node, not a kernel
+            "gpu_launches": (1 if T == BALANCED else 2) * args.steps,
             "clocks": clocks,
         }
         if tri is not None:
