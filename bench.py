@@ -596,6 +596,8 @@ def run_c5(args):
     cap = prompt + steps + 16
     model = Llama3DecodeModel.random_init(cfg, dev, torch.bfloat16, seed=1005,
                                           tp=TensorParallel(rank, world), max_positions=cap)
+    if args.tc_gemms is not None:
+        model.tc_projections = set(x for x in args.tc_gemms.split(",") if x)
     cache = model.make_cache(B, cap, page_size=P, shuffle_seed=1005 + rank)
     ids = torch.randint(0, cfg.vocab_size, (B, prompt),
                         generator=torch.Generator().manual_seed(1005)).to(dev)
@@ -708,6 +710,9 @@ def main():
                     help="also time the reference's Triton decode kernel (baseline/_ref)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of oracle CPU-baseline sampling at N=1 (0: skip)")
+    ap.add_argument("--tc-gemms", default=None,
+                    help="config 5: comma list of decode projections (qkv,o,gate_up,down) on "
+                         "the tcgen05 GEMM instead of cuBLAS (default: the model's choice)")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="N>1: weak = N x the config's batch, head-sharded (per-GPU work "
                          "fixed); strong = the config's batch split over N GPUs")

@@ -188,6 +188,25 @@ LLMC_API int llmc_rope_append_decode(const void* q, const void* k_new, const voi
                                      llmc_stream_t stream);
 
 /*
+ * llmc_rope_append_decode with q / k_new / v_new read in place from a wider buffer.
+ * Sequence b's query is at q + b * q_seq_stride elements, with its heads d apart.
+ * Its new key and value are at k_new / v_new + b * kv_seq_stride, also with heads d
+ * apart. The typical source is the [B, (Hq + 2 Hkv) * d] output of a fused QKV
+ * projection (attention.py:100-102 splits the same three views out of q/k/v_proj),
+ * which saves three copies per layer.
+ * Dense strides (Hq*d, Hkv*d) behave exactly as llmc_rope_append_decode. Other
+ * strides need the fused kernel's shapes (bf16/fp16, d in {64, 128, 256}) and get
+ * LLMC_EUNSUPPORTED otherwise.
+ */
+LLMC_API int llmc_rope_append_decode_strided(
+    const void* q, const void* k_new, const void* v_new, void* q_rot_out, void* k_pages,
+    void* v_pages, const int32_t* block_table, int32_t* seq_lens, const void* cos_tab,
+    const void* sin_tab, int rope_max_pos, void* out, float* part_o, float* part_lse,
+    int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d, int page_size,
+    int max_pages_per_seq, int num_pages, int partition_tokens, float scale, int dtype,
+    long long q_seq_stride, long long kv_seq_stride, llmc_stream_t stream);
+
+/*
  * Log-sum-exp merge of split-K partials into out [B, Hq, d].  For each (b, h)
  * with n = ceil(seq_lens[b] / partition_tokens) partitions: n >= 2 merges, n == 1
  * leaves out untouched (already written by llmc_paged_decode), n == 0 writes
@@ -260,6 +279,17 @@ LLMC_API const char* llmc_last_error_string(void);
 
 /* Library version string. */
 LLMC_API const char* llmc_version(void);
+
+/*
+ * Greedy pick of the decode loop: out[r] = argmax_j x[r, j] for x [rows, n] (first
+ * index of the maximum; NaN counts as the maximum, as torch.argmax).  Replaces
+ * torch.argmax(logits[:, -1, :], dim=-1) of src/llm_cuda/models/llama3/model.py:214.
+ * workspace: llmc_argmax_workspace_bytes(rows) bytes, 8-byte aligned, zero before
+ * the first call; every completed call leaves it at zero.  One launch.
+ */
+LLMC_API size_t llmc_argmax_workspace_bytes(int rows);
+LLMC_API int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype,
+                         void* workspace, llmc_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -41,10 +41,14 @@ SIGNATURES = {
     "llmc_paged_decode_noalloc": (_I, [_P] * 7 + [_I] * 8 + [_F, _I, _P]),
     "llmc_paged_decode_noalloc_capacity_bytes": (_SZ, []),
     "llmc_rope_append_decode": (_I, [_P] * 10 + [_I] + [_P] * 5 + [_I] * 8 + [_F, _I, _P]),
+    "llmc_rope_append_decode_strided": (_I, [_P] * 10 + [_I] + [_P] * 5 + [_I] * 8
+                                        + [_F, _I, ctypes.c_longlong, ctypes.c_longlong, _P]),
     "llmc_decode_gemm_workspace_bytes": (_SZ, [_I, _I, _I]),
     "llmc_decode_gemm": (_I, [_P, _P, _P, _P, _SZ, _P, _I, _I, _I, _P, _P]),
     "llmc_add_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _I, _P]),
     "llmc_swiglu": (_I, [_P, _P, _I, _I, _I, _P]),
+    "llmc_argmax_workspace_bytes": (_SZ, [_I]),
+    "llmc_argmax": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "llmc_last_error_string": (ctypes.c_char_p, []),
     "llmc_version": (ctypes.c_char_p, []),
 }

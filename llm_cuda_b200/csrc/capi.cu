@@ -27,7 +27,8 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
                                 int rope_max_pos, void* out, float* part_o, float* part_lse,
                                 int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
                                 int D, int P, int max_pages, int num_pages, int Tpart,
-                                float scale, int dtype, std::string* err, cudaStream_t stream);
+                                float scale, int dtype, std::string* err, cudaStream_t stream,
+                                long long q_stride, long long kv_stride);
 cudaError_t launch_decode_gemm(const void* x, const void* w, void* y, float* ws, size_t ws_floats,
                                int32_t* counters, int Mb, int N, int K, int32_t* status,
                                std::string* err, cudaStream_t stream);
@@ -39,6 +40,8 @@ cudaError_t launch_add_rmsnorm(void* x, const void* delta, const void* w, void* 
                                int hidden, float eps, int dtype, cudaStream_t stream);
 cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dtype,
                           cudaStream_t stream);
+cudaError_t launch_argmax(const void* x, int64_t* out, int rows, int n, int dtype,
+                          unsigned long long* keys, int* counters, int sms, cudaStream_t stream);
 }  // namespace llmc
 
 namespace {
@@ -182,14 +185,17 @@ int llmc_lse_merge(const float* part_o, const float* part_lse, const int32_t* se
   return LLMC_OK;
 }
 
-int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new, void* q_rot_out,
-                            void* k_pages, void* v_pages, const int32_t* block_table,
-                            int32_t* seq_lens, const void* cos_tab, const void* sin_tab,
-                            int rope_max_pos, void* out, float* part_o, float* part_lse,
-                            int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d,
-                            int page_size, int max_pages_per_seq, int num_pages,
-                            int partition_tokens, float scale, int dtype, llmc_stream_t stream) {
+int llmc_rope_append_decode_strided(
+    const void* q, const void* k_new, const void* v_new, void* q_rot_out, void* k_pages,
+    void* v_pages, const int32_t* block_table, int32_t* seq_lens, const void* cos_tab,
+    const void* sin_tab, int rope_max_pos, void* out, float* part_o, float* part_lse,
+    int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d, int page_size,
+    int max_pages_per_seq, int num_pages, int partition_tokens, float scale, int dtype,
+    long long q_seq_stride, long long kv_seq_stride, llmc_stream_t stream) {
   g_last_error.clear();
+  const bool dense = q_seq_stride == (long long)Hq * d && kv_seq_stride == (long long)Hkv * d;
+  if (q_seq_stride < (long long)Hq * d || kv_seq_stride < (long long)Hkv * d)
+    return fail(LLMC_EINVAL, "llmc_rope_append_decode: sequence strides smaller than Hq*d / Hkv*d");
   if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_rope_append_decode: unknown dtype");
   if (B < 0 || Hq <= 0 || Hkv <= 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
       num_pages <= 0 || partition_tokens < 0 || rope_max_pos <= 0)
@@ -214,7 +220,11 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
   cudaError_t e = llmc::launch_fused_decode(
       q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens, cos_tab, sin_tab,
       rope_max_pos, out, part_o, part_lse, lens_next, status, B, Hq, Hkv, d, page_size,
-      max_pages_per_seq, num_pages, partition_tokens, scale, dtype, &err, (cudaStream_t)stream);
+      max_pages_per_seq, num_pages, partition_tokens, scale, dtype, &err, (cudaStream_t)stream,
+      q_seq_stride, kv_seq_stride);
+  if (e == cudaErrorNotSupported && !dense)
+    return fail(LLMC_EUNSUPPORTED,
+                "llmc_rope_append_decode: strided q/k/v need the fused kernel's shapes");
   if (e == cudaErrorNotSupported) {
     // Shape outside the fused kernel: the same step with the separate kernels.
     cudaGetLastError();
@@ -247,6 +257,20 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
   }
   if (e != cudaSuccess) return cuda_fail(e, "llmc_rope_append_decode", err);
   return LLMC_OK;
+}
+
+int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new, void* q_rot_out,
+                            void* k_pages, void* v_pages, const int32_t* block_table,
+                            int32_t* seq_lens, const void* cos_tab, const void* sin_tab,
+                            int rope_max_pos, void* out, float* part_o, float* part_lse,
+                            int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d,
+                            int page_size, int max_pages_per_seq, int num_pages,
+                            int partition_tokens, float scale, int dtype, llmc_stream_t stream) {
+  return llmc_rope_append_decode_strided(
+      q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens, cos_tab, sin_tab,
+      rope_max_pos, out, part_o, part_lse, lens_next, status, B, Hq, Hkv, d, page_size,
+      max_pages_per_seq, num_pages, partition_tokens, scale, dtype, (long long)Hq * d,
+      (long long)Hkv * d, stream);
 }
 
 size_t llmc_decode_gemm_workspace_bytes(int Mb, int N, int K) {
@@ -295,6 +319,27 @@ int llmc_swiglu(const void* gate_up, void* out, int rows, int inter, int dtype,
   if (rows == 0) return LLMC_OK;
   cudaError_t e = llmc::launch_swiglu(gate_up, out, rows, inter, dtype, (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "llmc_swiglu");
+  return LLMC_OK;
+}
+
+size_t llmc_argmax_workspace_bytes(int rows) {
+  return rows > 0 ? (size_t)rows * (sizeof(unsigned long long) + sizeof(int)) : 0;
+}
+
+int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype, void* workspace,
+                llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_argmax: unknown dtype");
+  if (rows < 0 || n <= 0 || rows > 65535) return fail(LLMC_EINVAL, "llmc_argmax: bad sizes");
+  if (!x || !out || !workspace) return fail(LLMC_EINVAL, "llmc_argmax: NULL pointer argument");
+  if (reinterpret_cast<uintptr_t>(workspace) & 7)
+    return fail(LLMC_EINVAL, "llmc_argmax: workspace must be 8-byte aligned");
+  if (rows == 0) return LLMC_OK;
+  auto* keys = static_cast<unsigned long long*>(workspace);
+  int* counters = reinterpret_cast<int*>(keys + rows);
+  cudaError_t e = llmc::launch_argmax(x, out, rows, n, dtype, keys, counters,
+                                      llmc::balanced_grid(), (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_argmax");
   return LLMC_OK;
 }
 

@@ -12,8 +12,18 @@
 //               fp32 accumulate in TMEM) from shared-memory descriptors and returns
 //               each stage with tcgen05.commit on its "empty" mbarrier;
 //   warps 2-5   epilogue: tcgen05.ld 32x32b of their TMEM lane quarter (lane = output
-//               feature, column = batch row), then bf16 stores, or fp32 reductions
-//               into an L2-resident accumulator when K is split across CTAs.
+//               feature, column = batch row), then bf16 stores.
+//
+// Work split, by shape:
+//   * stream-K (N / 128 >= 74 tiles): CTA c takes units [c*W/G, (c+1)*W/G) of the
+//     W = tiles * k-chunks units; a tile shared by several CTAs is summed from fp32
+//     parts by the CTA that completes it (global slots + a self-resetting counter).
+//   * cluster split-K (fewer tiles): a cluster of S CTAs (S <= 8) owns one tile, each
+//     CTA a 1/S slice of K; the S accumulators are summed through distributed shared
+//     memory behind two cluster barriers, with no global round trip.
+// Programmatic dependent launch: the weights never depend on the previous kernel, so
+// the first ring stages of W are requested before griddepcontrol.wait and only the
+// activation loads (and every global write) wait for the predecessor.
 //
 // D = A . B^T with A = W tile (K-major), B = x tile (K-major), so D^T = y tile.
 // Every mbarrier wait is bounded; TMEM is always released.
@@ -86,7 +96,26 @@ struct Params {
   int Mb, N, K;
   long long units;     // tiles * k-chunks
   int max_seg;         // slots per tile
+  int cluster;         // cluster split-K: CTAs per tile (0: stream-K)
 };
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory offset in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t local_addr, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+  return remote;
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t remote_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote_addr), "f"(v) : "memory");
+}
 
 // Ring depth that fits 227 KB of shared memory for a batch tile of NB rows.
 template <int NB, int CPS>
@@ -136,7 +165,18 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int KC = p.K / (kChunk * CPS);   // work units (stages) per tile
   const long long W = p.units, G = gridDim.x;
-  const long long u0 = sk_start(blockIdx.x, W, G), u1 = sk_start(blockIdx.x + 1, W, G);
+  const bool cl = p.cluster > 0;
+  long long u0, u1;
+  uint32_t crank = 0;
+  if (cl) {   // cluster split-K: tile blockIdx.x / S, K slice of this CTA's cluster rank
+    crank = cluster_ctarank();
+    const long long tile = blockIdx.x / p.cluster;
+    u0 = tile * KC + (long long)crank * KC / p.cluster;
+    u1 = tile * KC + ((long long)crank + 1) * KC / p.cluster;
+  } else {
+    u0 = sk_start(blockIdx.x, W, G);
+    u1 = sk_start(blockIdx.x + 1, W, G);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -166,11 +206,34 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  pdl_launch_dependents();
+  float acc_lo[32], acc_hi[32];   // cluster split-K: this thread's accumulator row
   if (warp == 0) {
     // ---- TMA producer: every k-chunk of this CTA's range, across tile boundaries ----
     if (lane == 0) {
-      int i = 0;
-      for (long long u = u0; u < u1; ++u, ++i) {
+      // The first ring-full of weight boxes goes out before waiting for the previous
+      // kernel (weights are never written by it); the activation boxes follow the wait.
+      const long long pre = (u1 - u0) < kStages ? (u1 - u0) : kStages;
+      for (long long i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const uint32_t fb = smem_u32(&full_bar[i]);
+        mbar_arrive_expect_tx(fb, STAGE);
+        const int tile = (int)(u / KC), kc = (int)(u % KC) * CPS;
+        const uint32_t a = smem_u32(smem + i * STAGE);
+#pragma unroll
+        for (int j = 0; j < CPS; ++j) tma_load_2d(a + j * A1, &tmap_w, (kc + j) * kChunk, tile * kTileN, fb);
+      }
+      pdl_wait();
+      for (long long i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        const uint32_t fb = smem_u32(&full_bar[i]);
+        const int kc = (int)(u % KC) * CPS;
+        const uint32_t a = smem_u32(smem + i * STAGE);
+#pragma unroll
+        for (int j = 0; j < CPS; ++j) tma_load_2d(a + A_BYTES + j * B1, &tmap_x, (kc + j) * kChunk, 0, fb);
+      }
+      int i = (int)pre;
+      for (long long u = u0 + pre; u < u1; ++u, ++i) {
         const int s = i % kStages;
         const uint32_t round = i / kStages;
         mbar_wait_bounded(smem_u32(&empty_bar[s]), (round & 1u) ^ 1u, abort_flag, p.status);
@@ -225,8 +288,20 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   } else {
     // ---- Epilogue: warps 2..5 own TMEM lane quarters (warp % 4) * 32 ----
     const int quarter = warp & 3;
+    pdl_wait();   // global writes come after the predecessor grid (y / ws may alias its data)
     int seg = 0;
     long long u = u0;
+    if (cl) {
+      // Cluster split-K (NB = 64): the accumulator row of this thread stays in
+      // registers until every CTA of the cluster is past its MMAs (first cluster
+      // barrier below); then each value is pushed into the shared memory of the CTA
+      // that sums that row.
+      mbar_wait_bounded(smem_u32(&tfull_bar[0]), 0u, abort_flag, p.status);
+      tc_fence_after();
+      tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16), acc_lo);
+      tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + 32u, acc_hi);
+      u = u1;   // nothing left for the stream-K loop
+    }
     while (u < u1) {
       const int tile = (int)(u / KC);
       const long long tile_end = (long long)(tile + 1) * KC;
@@ -285,11 +360,20 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             float t[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) t[j] = 0.f;
-            for (int sl = 0; sl < nseg; ++sl) {
-              const float* src = base + ((size_t)sl * NB + b0) * kTileN;
+            // Up to 4 parts' loads in flight together: one L2 round trip per 4 parts.
+            for (int s0 = 0; s0 < nseg; s0 += 4) {
+              float v[4][32];
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (b0 + j < p.Mb) t[j] += __ldcg(src + (size_t)j * kTileN);
+              for (int q = 0; q < 4; ++q) {
+                const float* src = base + ((size_t)(s0 + q) * NB + b0) * kTileN;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  v[q][j] = (s0 + q < nseg && b0 + j < p.Mb) ? __ldcg(src + (size_t)j * kTileN) : 0.f;
+              }
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int j = 0; j < 32; ++j) t[j] += v[q][j];
             }
             if (ok) {
 #pragma unroll
@@ -302,6 +386,51 @@ decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
       }
       u = e;
       ++seg;
+    }
+  }
+  __syncwarp();
+  if (cl) {
+    // CTA rank q sums rows [q*128/S, (q+1)*128/S) of the tile.  Its receive buffer
+    // (the idle ring) holds [S source ranks][64 columns][LR rows]; stores from the
+    // peers are fire-and-forget, the second barrier makes them visible, and the sum
+    // then reads local shared memory only.
+    const int S = p.cluster;                 // 2, 4 or 8: every CTA sums 128 / S rows
+    const int LR = kTileN / S;
+    const uint32_t buf = smem_u32(smem);
+    cluster_sync_all();   // every CTA's MMAs are done: its ring may be overwritten
+    if (warp >= 2) {
+      const int row = (warp & 3) * 32 + lane;
+      const int q = row / LR;                        // owner of this row
+      const int lr = row - q * LR;
+      const uint32_t dst = dsmem_addr(buf, (uint32_t)q) +
+                           (uint32_t)((crank * NB) * LR + lr) * 4u;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) st_dsmem_f32(dst + (uint32_t)(c * LR) * 4u, acc_lo[c]);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) st_dsmem_f32(dst + (uint32_t)((32 + c) * LR) * 4u, acc_hi[c]);
+    }
+    cluster_sync_all();   // all pushes have landed
+    if (!*abort_flag) {
+      // All six warps: item = (batch row b, 4 consecutive rows of this CTA's share),
+      // S float4 reads of local shared memory and one 8-byte bf16x4 store.
+      const int tile = (int)(blockIdx.x / S);
+      const float* rb = reinterpret_cast<const float*>(smem);
+      __nv_bfloat16* ybase = p.y + tile * kTileN + crank * LR;
+      const int g4 = LR / 4, items = g4 * p.Mb;
+      for (int it = threadIdx.x; it < items; it += kThreads) {
+        const int b = it / g4, lr = (it - b * g4) * 4;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < S; ++q) {
+          const float4 v = *reinterpret_cast<const float4*>(rb + (q * NB + b) * LR + lr);
+          a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+        }
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x, a.y);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(a.z, a.w);
+        uint2 pk;
+        pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+        pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(ybase + (size_t)b * p.N + lr) = pk;
+      }
     }
   }
   tc_fence_before();
@@ -396,14 +525,53 @@ static cudaError_t launch_gemm_nb(const void* x, const void* w, void* y, float* 
   p.counters = counters;
   p.status = status;
   p.Mb = Mb; p.N = N; p.K = K;
-  p.units = (long long)(N / gemm::kTileN) * (K / (gemm::kChunk * CPS));
-  const int grid = (int)(p.units < sms ? p.units : sms);
-  p.max_seg = gemm_max_segments(N / gemm::kTileN, K / (gemm::kChunk * CPS), grid);
-  if ((size_t)(N / gemm::kTileN) * p.max_seg * NB * gemm::kTileN > ws_floats) {
-    *err = "decode GEMM workspace too small";
-    return cudaErrorInvalidValue;
+  const int tiles = N / gemm::kTileN, kc = K / (gemm::kChunk * CPS);
+  p.units = (long long)tiles * kc;
+  // Cluster split-K when the tiles leave most SMs idle: csz CTAs per tile, csz <= 8, as
+  // many as fit the SMs and the co-resident cluster count.
+  int csz = NB == 64 ? sms / tiles : 1;   // the cluster path keeps a 64-column row in registers
+  if (csz > 8) csz = 8;
+  if (csz > kc) csz = kc;
+  csz = csz >= 8 ? 8 : (csz >= 4 ? 4 : (csz >= 2 ? 2 : 1));   // a power of two dividing 128
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(gemm::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  while (csz >= 2) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = csz;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(tiles * csz);
+    cfg.numAttrs = 2;
+    int nclusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&nclusters, kern, &cfg) == cudaSuccess &&
+        nclusters >= tiles)
+      break;
+    cudaGetLastError();
+    csz /= 2;
   }
-  kern<<<grid, gemm::kThreads, smem, stream>>>(mw, mx, p);
+  if (csz >= 2) {
+    p.cluster = csz;
+    p.max_seg = 1;
+  } else {
+    p.cluster = 0;
+    cfg.numAttrs = 1;
+    const int grid = (int)(p.units < sms ? p.units : sms);
+    cfg.gridDim = dim3(grid);
+    p.max_seg = gemm_max_segments(tiles, kc, grid);
+    if ((size_t)tiles * p.max_seg * NB * gemm::kTileN > ws_floats) {
+      *err = "decode GEMM workspace too small";
+      return cudaErrorInvalidValue;
+    }
+  }
+  e = cudaLaunchKernelEx(&cfg, kern, mw, mx, p);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 

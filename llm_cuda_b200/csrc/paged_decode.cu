@@ -76,8 +76,8 @@ struct Params {
   // sequence b sits at position seq_lens[b] (lengths before the append): its q and k
   // are rotated here with cos/sin row pos, k/v are written to the pages, and the
   // advanced lengths go to lens_next (published into seq_lens by the merge kernel).
-  const void* k_new;       // [B, Hkv, D]
-  const void* v_new;       // [B, Hkv, D]
+  const void* k_new;       // [B, Hkv, D], sequence b at k_new + b * kv_stride
+  const void* v_new;       // [B, Hkv, D], same strides as k_new
   const void* cos_tab;     // [rope_max_pos, D]
   const void* sin_tab;
   void* k_pages;           // pools written with the new token
@@ -96,6 +96,8 @@ struct Params {
   int balanced;
   int cap_chunks;
   int32_t* counters;       // [rows + 1], zero between calls
+  long long q_stride;      // elements between the queries of consecutive sequences
+  long long kv_stride;     // the same for k_new / v_new (heads are D apart in both)
   int32_t* seq_lens_out;   // FUSE + balanced: lengths after the step are written here
 };
 
@@ -601,7 +603,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
                     uint32_t (&sn)[KH][2]) {
     const int ghead = it.hg * 8 + g;
     const bool ok = ghead < p.G;
-    const T* qrow = qbase + ((size_t)it.b * p.Hq + (ok ? it.kvh * p.G + ghead : 0)) * D;
+    const T* qrow = qbase + (size_t)it.b * p.q_stride + (size_t)(ok ? it.kvh * p.G + ghead : 0) * D;
 #pragma unroll
     for (int kc = 0; kc < KC; ++kc) {
       dst[kc][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qrow + kc * 16 + 2 * c)) : 0u;
@@ -634,8 +636,8 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   };
   auto fetch_newtok = [&](const Piece& x, NewTok& nt) {
     const int pos = x.L - 1;
-    const T* kn = reinterpret_cast<const T*>(p.k_new) + ((size_t)x.b * p.Hkv + x.kvh) * D;
-    const T* vn = reinterpret_cast<const T*>(p.v_new) + ((size_t)x.b * p.Hkv + x.kvh) * D;
+    const T* kn = reinterpret_cast<const T*>(p.k_new) + (size_t)x.b * p.kv_stride + (size_t)x.kvh * D;
+    const T* vn = reinterpret_cast<const T*>(p.v_new) + (size_t)x.b * p.kv_stride + (size_t)x.kvh * D;
     const T* crow = reinterpret_cast<const T*>(p.cos_tab) + (size_t)pos * D;
     const T* srow = reinterpret_cast<const T*>(p.sin_tab) + (size_t)pos * D;
     nt.page = __ldg(p.block_table + (size_t)x.b * p.max_pages + pos / p.P);
@@ -1365,13 +1367,15 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
                                 int rope_max_pos, void* out, float* part_o, float* part_lse,
                                 int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
                                 int D, int P, int max_pages, int num_pages, int Tpart,
-                                float scale, int dtype, std::string* err, cudaStream_t stream) {
+                                float scale, int dtype, std::string* err, cudaStream_t stream,
+                                long long q_stride, long long kv_stride) {
   if (B == 0) return cudaSuccess;
   if (!fast_path_applies(dtype, D, P, max_pages, Tpart, B, q_raw, kp, vp))
     return cudaErrorNotSupported;
   const int G = Hq / Hkv;
   fast::Params p;
   p.q = q_raw; p.out = out; p.block_table = bt;
+  p.q_stride = q_stride; p.kv_stride = kv_stride;
   p.seq_lens = seq_lens; p.status = status;
   p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
   p.max_pages = max_pages; p.num_pages = num_pages;
@@ -1405,6 +1409,7 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
   if (fast_ok) {
     fast::Params p;
     p.q = q; p.out = out; p.block_table = bt;
+    p.q_stride = (long long)Hq * D; p.kv_stride = 0;
     p.seq_lens = seq_lens; p.status = status;
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
     p.max_pages = max_pages; p.num_pages = num_pages;

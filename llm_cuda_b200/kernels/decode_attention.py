@@ -303,12 +303,27 @@ def rope_append_decode(
         raise ValueError("q/k/v shapes do not match the cache layout")
     if key_pages.dtype != q.dtype or k.dtype != q.dtype or cos.dtype != q.dtype:
         raise ValueError("q, k, v, pages and the RoPE table must share a dtype")
-    q = q.contiguous()
-    k = k.contiguous()
-    v = v.contiguous()
     max_pages = block_table.shape[1]
     if partition_tokens is None:
         partition_tokens = BALANCED
+    # q/k/v may be views into one fused QKV projection output ([B, 1, (Hq+2Hkv)*d]
+    # split into heads): read in place when only the sequence stride is not dense.
+    def seq_stride(t, H):
+        if t.dim() == 4 and t.shape[2] != 1:
+            return None
+        if t.stride(-1) != 1 or (H > 1 and t.stride(1) != d):
+            return None
+        return t.stride(0)
+    qs, ks, vs = seq_stride(q, Hq), seq_stride(k, Hkv), seq_stride(v, Hkv)
+    strided = (qs is not None and ks is not None and ks == vs and partition_tokens == BALANCED
+               and (qs, ks) != (Hq * d, Hkv * d)
+               and lib.llmc_decode_balanced_supported(q.data_ptr(), key_pages.data_ptr(),
+                                                      value_pages.data_ptr(),
+                                                      N.dtype_code(q.dtype), d, P, max_pages, B))
+    if not strided:
+        q = q.contiguous()
+        k = k.contiguous()
+        v = v.contiguous()
     if scale is None:
         scale = 1.0 / math.sqrt(d)
     out = torch.empty(B, Hq, d, dtype=q.dtype, device=q.device) if out is None else out
@@ -321,12 +336,15 @@ def rope_append_decode(
     st = status if status is not None else default_status(q.device)
     if events is not None:
         events[0].record()
-    rc = lib.llmc_rope_append_decode(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), q_out.data_ptr(), key_pages.data_ptr(),
-        value_pages.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(), cos.data_ptr(),
-        sin.data_ptr(), cos.shape[0], out.data_ptr(), N.ptr(part_o), N.ptr(part_lse),
-        ws.lens_next(B).data_ptr(), st.data_ptr(), B, Hq, Hkv, d, P, max_pages, num_pages,
-        partition_tokens, float(scale), N.dtype_code(q.dtype), N.stream_handle(q.device))
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), q_out.data_ptr(), key_pages.data_ptr(),
+            value_pages.data_ptr(), block_table.data_ptr(), seq_lens.data_ptr(), cos.data_ptr(),
+            sin.data_ptr(), cos.shape[0], out.data_ptr(), N.ptr(part_o), N.ptr(part_lse),
+            ws.lens_next(B).data_ptr(), st.data_ptr(), B, Hq, Hkv, d, P, max_pages, num_pages,
+            partition_tokens, float(scale), N.dtype_code(q.dtype))
+    if strided:
+        rc = lib.llmc_rope_append_decode_strided(*args, qs, ks, N.stream_handle(q.device))
+    else:
+        rc = lib.llmc_rope_append_decode(*args, N.stream_handle(q.device))
     if events is not None:   # brackets the decode and merge launches of the step
         events[1].record()
     N.check(rc, "llmc_rope_append_decode")

@@ -82,3 +82,26 @@ def decode_gemm(x: torch.Tensor, w: torch.Tensor, status: torch.Tensor | None = 
                                    N.stream_handle(x.device))
     N.check(rc, "llmc_decode_gemm")
     return y.view(*x.shape[:-1], n_out)
+
+
+_argmax_ws: dict = {}
+
+
+def argmax_rows(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``torch.argmax(x, dim=-1)`` of a 2-D CUDA tensor in one launch (the greedy pick
+    of the decode loop, ``model.py:214``): first index of the maximum, int64."""
+    if x.dim() != 2:
+        raise ValueError("argmax_rows takes a 2-D tensor")
+    x = x.contiguous()
+    rows, n = x.shape
+    out = torch.empty(rows, dtype=torch.int64, device=x.device) if out is None else out
+    key = (x.device.index, rows)
+    ws = _argmax_ws.get(key)
+    if ws is None:   # zero once; the kernel leaves it at zero
+        nbytes = N.load().llmc_argmax_workspace_bytes(rows)
+        ws = torch.zeros(max((nbytes + 7) // 8, 1), dtype=torch.int64, device=x.device)
+        _argmax_ws[key] = ws
+    rc = N.load().llmc_argmax(x.data_ptr(), out.data_ptr(), rows, n, N.dtype_code(x.dtype),
+                              ws.data_ptr(), N.stream_handle(x.device))
+    N.check(rc, "llmc_argmax")
+    return out

@@ -31,9 +31,16 @@ from dataclasses import dataclass
 import torch
 import torch.nn.functional as F
 
-from ...kernels.step_ops import add_rmsnorm, decode_gemm, swiglu
+from ...kernels.step_ops import add_rmsnorm, argmax_rows, decode_gemm, swiglu
 from .kv_cache import PagedKVCache, make_block_table
 from .rotary import RopeTable
+
+
+# Layer projections of the decode step served by the tcgen05 decode GEMM by default.
+# Measured at B=64 inside the whole-step graph, cuBLAS is still ahead on the layer
+# shapes (qkv 11.0 vs 14.6 us, gate_up 41.6 vs 48.5 us), so none are by default; the
+# vocabulary projection (lm_head) always uses the tcgen05 GEMM, which is faster there.
+DEFAULT_TC_PROJECTIONS = ()
 
 
 @dataclass
@@ -106,6 +113,8 @@ class Llama3DecodeModel:
         # Optional replacement of the attention core ``(layer, q, k, v, layer_cache) -> out``
         # taking the raw (un-rotated) q/k/v; tests of the TP plumbing on CPU ranks use it.
         self.attn_core = None
+        # Decode projections that run on the tcgen05 decode GEMM (the rest: F.linear).
+        self.tc_projections = set(DEFAULT_TC_PROJECTIONS)
 
     # -- weights ---------------------------------------------------------------
     def _add_layer(self, full: dict) -> None:
@@ -205,13 +214,23 @@ class Llama3DecodeModel:
         return q, k, v
 
     def _mlp(self, L: dict, x: torch.Tensor) -> torch.Tensor:
-        gu = F.linear(x, L["wgu"])
+        gu = self._linear(x, L["wgu"], "gate_up")
         if gu.is_cuda:
             h = swiglu(gu)                                 # fused CUDA kernel
         else:
             gate, up = gu.split(self.inter, dim=-1)
             h = (gate * torch.sigmoid(gate)) * up         # swiglu.py:103-107
-        return self.tp.all_reduce_(F.linear(h, L["wdown"]))
+        return self.tp.all_reduce_(self._linear(h, L["wdown"], "down"))
+
+    def _linear(self, x: torch.Tensor, w: torch.Tensor, name: str) -> torch.Tensor:
+        """``x @ w.T`` for the projection ``name``: the tcgen05 decode GEMM when ``name``
+        is in ``self.tc_projections`` and the shape qualifies, else ``F.linear``."""
+        K = x.shape[-1]
+        rows = x.numel() // K
+        if (name in self.tc_projections and x.is_cuda and x.dtype == torch.bfloat16
+                and rows <= 256 and w.shape[0] % 128 == 0 and K % 64 == 0):
+            return decode_gemm(x.reshape(rows, K), w).view(*x.shape[:-1], w.shape[0])
+        return F.linear(x, w)
 
     def _lm_head(self, h: torch.Tensor) -> torch.Tensor:
         """Vocabulary projection.  At decode batch sizes the 1 GB bf16 weight streams
@@ -269,7 +288,7 @@ class Llama3DecodeModel:
         for li, L in enumerate(self.layers):
             lc = cache.get_layer(li)
             x, h = self._add_norm(x, L["in_norm"], delta)
-            q, k, v = self._split_qkv(F.linear(h, L["wqkv"]), B, 1)
+            q, k, v = self._split_qkv(self._linear(h, L["wqkv"], "qkv"), B, 1)
             if self.attn_core is not None:
                 attn = self.attn_core(li, q, k, v, lc)
             else:
@@ -277,7 +296,7 @@ class Llama3DecodeModel:
                 attn = lc.rope_append_decode(q, k, v, self.rope,
                                              partition_tokens=partition_tokens)
             attn = attn.reshape(B, 1, self.hq * cfg.head_dim)
-            o = self.tp.all_reduce_(F.linear(attn, L["wo"]))
+            o = self.tp.all_reduce_(self._linear(attn, L["wo"], "o"))
             x, h = self._add_norm(x, L["post_norm"], o)
             delta = self._mlp(L, h)
         x, h = self._add_norm(x, self.final_norm, delta)
@@ -310,7 +329,8 @@ class DecodeGraph:
         # warm-up (allocates workspaces outside the capture), then undo its append
         lens0 = cache.get_layer(0).seq_lens.clone()
         host0 = list(cache.get_layer(0).host_lengths)
-        model.decode_step(self.ids, cache, partition_tokens)
+        warm = model.decode_step(self.ids, cache, partition_tokens)
+        argmax_rows(warm)                       # its workspace exists before the capture
         torch.cuda.synchronize()
         self._reset(lens0, host0)
         s = torch.cuda.Stream(device=model.device)
@@ -319,7 +339,7 @@ class DecodeGraph:
         with torch.cuda.stream(s):
             with torch.cuda.graph(self.graph, stream=s):
                 self.logits = model.decode_step(self.ids, cache, partition_tokens)
-                self.next_ids.copy_(torch.argmax(self.logits, dim=-1))
+                argmax_rows(self.logits, out=self.next_ids)
                 self.ids.copy_(self.next_ids)
         torch.cuda.current_stream(model.device).wait_stream(s)
         torch.cuda.synchronize()

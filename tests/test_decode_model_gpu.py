@@ -142,14 +142,15 @@ def test_decode_graph_replay_matches_eager():
     assert torch.equal(run(True), run(False))
 
 
+@pytest.mark.parametrize("hidden", [4096, 8192 + 8, 100])   # 16-byte vectors x1 / x4; scalar
 @pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-5), (torch.bfloat16, 2e-2)])
-def test_add_rmsnorm_and_swiglu_match_torch_fp32(dtype, tol):
+def test_add_rmsnorm_and_swiglu_match_torch_fp32(dtype, tol, hidden):
     from llm_cuda_b200.kernels.step_ops import add_rmsnorm, swiglu
 
     g = torch.Generator(device=DEV).manual_seed(3)
-    x = torch.randn(64, 1, 4096, device=DEV, generator=g).to(dtype)
-    dl = torch.randn(64, 1, 4096, device=DEV, generator=g).to(dtype)
-    w = (1 + 0.1 * torch.randn(4096, device=DEV, generator=g)).to(dtype)
+    x = torch.randn(64, 1, hidden, device=DEV, generator=g).to(dtype)
+    dl = torch.randn(64, 1, hidden, device=DEV, generator=g).to(dtype)
+    w = (1 + 0.1 * torch.randn(hidden, device=DEV, generator=g)).to(dtype)
     xs = (x.float() + dl.float()).to(dtype).float()          # residual stream in the dtype
     ref = xs * torch.rsqrt(xs.pow(2).mean(-1, keepdim=True) + 1e-5) * w.float()
     h = add_rmsnorm(x, w, 1e-5, delta=dl)
@@ -158,3 +159,47 @@ def test_add_rmsnorm_and_swiglu_match_torch_fp32(dtype, tol):
     gu = torch.randn(64, 1, 2 * 1792, device=DEV, generator=g).to(dtype)
     gg, uu = gu.float().split(1792, -1)
     torch.testing.assert_close(swiglu(gu).float(), gg * torch.sigmoid(gg) * uu, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,n", [(64, 128256), (3, 1000), (1, 7)])
+def test_argmax_rows_matches_torch(dtype, rows, n):
+    from llm_cuda_b200.kernels.step_ops import argmax_rows
+
+    g = torch.Generator(device=DEV).manual_seed(rows + n)
+    x = torch.randn(rows, n, device=DEV, generator=g).to(dtype)
+    x[0, n // 2] = x[0, n // 3] = 100.0          # a tie: the first index wins
+    for _ in range(2):                             # the workspace returns to zero
+        got = argmax_rows(x)
+        torch.testing.assert_close(got, torch.argmax(x, dim=-1))
+    assert int(got[0]) == n // 3
+
+
+def test_fused_step_reads_strided_qkv_views():
+    """q/k/v as views into one fused QKV projection output (decode_step's layout) give
+    the same step, bit for bit, as contiguous copies."""
+    from llm_cuda_b200.models.llama3 import PagedKVLayerCache, RopeTable, make_block_table
+
+    B, Hq, Hkv, d, P, L = 8, 32, 8, 128, 16, 777
+    mp = (L + 64) // P
+    gen = torch.Generator().manual_seed(5)
+    bt = make_block_table(B, mp, B * mp + 3, mp, generator=gen)
+    out = []
+    qkv = torch.randn(B, 1, (Hq + 2 * Hkv) * d, device=DEV,
+                      generator=torch.Generator(device=DEV).manual_seed(6)).bfloat16()
+    q, k, v = qkv.split([Hq * d, Hkv * d, Hkv * d], dim=-1)
+    views = [t.view(B, 1, h, d).transpose(1, 2) for t, h in ((q, Hq), (k, Hkv), (v, Hkv))]
+    for strided in (True, False):
+        c = PagedKVLayerCache(Hkv, d, mp * P, P, DEV, torch.bfloat16, batch_size=B,
+                              num_pages=B * mp + 3, block_table=bt)
+        gd = torch.Generator(device=DEV).manual_seed(7)
+        c.key_pages.normal_(generator=gd)
+        c.value_pages.normal_(generator=gd)
+        c.seq_lens.fill_(L)
+        c.host_lengths = [L] * B
+        rope = RopeTable(mp * P, d, 500000.0, DEV, torch.bfloat16)
+        qq, kk, vv = views if strided else [t.contiguous() for t in views]
+        out.append((c.rope_append_decode(qq, kk, vv, rope).clone(), c.key_pages.clone()))
+        c.check_status()
+    assert torch.equal(out[0][0], out[1][0])
+    assert torch.equal(out[0][1], out[1][1])
