@@ -234,8 +234,55 @@ cudaError_t launch_add_rmsnorm(void* x, const void* delta, const void* w, void* 
   return cudaGetLastError();
 }
 
+// 16-byte vectors: thread i handles elements [VEC*i, VEC*i + VEC) of the [rows, inter]
+// output (inter % VEC == 0, so a vector never crosses a row).
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_vec_kernel(const T* __restrict__ gu,
+                                                         T* __restrict__ out, int inter,
+                                                         long long nvec) {
+  constexpr int VEC = 16 / sizeof(T);
+  pdl_launch_dependents();
+  pdl_wait();
+  const int vpr = inter / VEC;   // vectors per row
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nvec;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / vpr;
+    const int cv = (int)(i - row * vpr);
+    const uint4 g = __ldg(reinterpret_cast<const uint4*>(gu + row * 2 * inter) + cv);
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(gu + row * 2 * inter + inter) + cv);
+    const T* ge = reinterpret_cast<const T*>(&g);
+    const T* ue = reinterpret_cast<const T*>(&u);
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float gv = to_f32(ge[e]);
+      oe[e] = from_f32<T>(gv / (1.f + expf(-gv)) * to_f32(ue[e]));
+    }
+    reinterpret_cast<uint4*>(out)[i] = o;
+  }
+}
+
+template <typename T>
+static bool launch_swiglu_vec(const void* gu, void* out, int rows, int inter,
+                              cudaStream_t stream) {
+  constexpr int VEC = 16 / sizeof(T);
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (inter % VEC || !al(gu) || !al(out)) return false;
+  const long long nvec = (long long)rows * inter / VEC;
+  const int grid = (int)((nvec + 255) / 256 < 148 * 8 ? (nvec + 255) / 256 : 148 * 8);
+  launch_pdl(swiglu_vec_kernel<T>, dim3(grid), dim3(256), stream, (const T*)gu, (T*)out, inter,
+             nvec);
+  return true;
+}
+
 cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dtype,
                           cudaStream_t stream) {
+  bool done;
+  if (dtype == LLMC_F32) done = launch_swiglu_vec<float>(gu, out, rows, inter, stream);
+  else if (dtype == LLMC_F16) done = launch_swiglu_vec<__half>(gu, out, rows, inter, stream);
+  else done = launch_swiglu_vec<__nv_bfloat16>(gu, out, rows, inter, stream);
+  if (done) return cudaGetLastError();
   const long long total = (long long)rows * inter;
   const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
   if (dtype == LLMC_F32)

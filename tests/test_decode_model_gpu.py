@@ -156,8 +156,9 @@ def test_add_rmsnorm_and_swiglu_match_torch_fp32(dtype, tol, hidden):
     h = add_rmsnorm(x, w, 1e-5, delta=dl)
     torch.testing.assert_close(x.float(), xs)
     torch.testing.assert_close(h.float(), ref, rtol=tol, atol=tol)
-    gu = torch.randn(64, 1, 2 * 1792, device=DEV, generator=g).to(dtype)
-    gg, uu = gu.float().split(1792, -1)
+    inter = hidden * 7 // 16                 # 1792: 16-byte vectors; 3587, 43: scalar path
+    gu = torch.randn(64, 1, 2 * inter, device=DEV, generator=g).to(dtype)
+    gg, uu = gu.float().split(inter, -1)
     torch.testing.assert_close(swiglu(gu).float(), gg * torch.sigmoid(gg) * uu, rtol=tol, atol=tol)
 
 
