@@ -598,6 +598,8 @@ def run_c5(args):
                                           tp=TensorParallel(rank, world), max_positions=cap)
     if args.tc_gemms is not None:
         model.tc_projections = set(x for x in args.tc_gemms.split(",") if x)
+    if world > 1 and not args.nccl_allreduce:
+        model.enable_fused_allreduce(rows_cap=B)   # one-shot NVLink AR + add + RMSNorm
     cache = model.make_cache(B, cap, page_size=P, shuffle_seed=1005 + rank)
     ids = torch.randint(0, cfg.vocab_size, (B, prompt),
                         generator=torch.Generator().manual_seed(1005)).to(dev)
@@ -674,8 +676,9 @@ def run_c5(args):
             "config": {"workload": "config5 Llama-3-8B-shaped decode: 32 layers, hidden 4096, "
                                    "Hq32 Hkv8 d128, ffn 14336, vocab 128256, B64, KV prefilled "
                                    "to 2048 (page 16), greedy decode",
-                       "parallelism": f"tp{world} (head-sharded, NCCL all-reduce after "
-                                      "o_proj/down_proj)",
+                       "parallelism": f"tp{world} (head-sharded; " + (
+                           "fused one-shot NVLink all-reduce + add + RMSNorm" if model.tp.fused
+                           is not None else "NCCL all-reduce") + " after o_proj/down_proj)",
                        "partition_tokens": "balanced", "graph": "whole step (32 layers + lm_head + "
                                                        "argmax) replayed from one CUDA graph",
                        "weight_bytes_per_rank": w_bytes,
@@ -713,6 +716,9 @@ def main():
     ap.add_argument("--tc-gemms", default=None,
                     help="config 5: comma list of decode projections (qkv,o,gate_up,down) on "
                          "the tcgen05 GEMM instead of cuBLAS (default: the model's choice)")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="config 5 at N>1: NCCL all-reduce + add/RMSNorm kernel instead of the "
+                         "fused one-shot NVLink kernel")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="N>1: weak = N x the config's batch, head-sharded (per-GPU work "
                          "fixed); strong = the config's batch split over N GPUs")

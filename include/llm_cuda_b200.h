@@ -291,6 +291,46 @@ LLMC_API size_t llmc_argmax_workspace_bytes(int rows);
 LLMC_API int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype,
                          void* workspace, llmc_stream_t stream);
 
+/*
+ * Tensor-parallel decode: one-shot all-reduce over NVLink peer memory fused with the
+ * residual add and RMSNorm.  Replaces the all-reduce of the row-parallel o_proj /
+ * down_proj partials (src/llm_cuda/parallel/tensor_parallel.py:83-90) and the
+ * residual add + RMSNorm after it (src/llm_cuda/models/llama3/model.py:37-42,
+ * norm.py:31-33).  No counterpart in the reference, which sums the partials in one
+ * process.
+ *
+ * Setup (once per TP group):
+ *  - Every rank allocates two shared regions with llmc_ipc_alloc: recv of
+ *    llmc_ar_region_bytes bytes, and flags of *flag_bytes bytes (both zero-filled).
+ *  - The ranks exchange the llmc_ipc_handle_bytes()-byte handles, e.g. with
+ *    torch.distributed.all_gather_object, and open the peers' with llmc_ipc_open.
+ *  - Each rank builds two device arrays [world], recv_ptrs and flag_ptrs: rank q's
+ *    pointers, its own included.
+ *  - epoch is a zeroed int32 [rows_cap] on the rank's own GPU.
+ *
+ * Per call, on every rank with the same rows:
+ *   sum = sum over ranks of partial (fp32 in rank order, rounded to the dtype);
+ *   x += sum (rounded to the dtype); out = x * rsqrt(mean(x^2) + eps) * weight.
+ * One launch, one CTA per row. A row pushes its partial to every rank, publishes its
+ * epoch with a system-scope release, and waits, bounded at 2 s, for every rank's
+ * row. On timeout LLMC_STATUS_WAIT_TIMEOUT is set and the row is left unchanged; the
+ * epochs are then out of step, so rebuild the regions. Calls must be issued in the
+ * same order on all ranks.
+ */
+LLMC_API size_t llmc_ipc_handle_bytes(void);
+LLMC_API int llmc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);
+LLMC_API int llmc_ipc_open(const void* handle, void** dev_ptr);
+LLMC_API int llmc_ipc_close(void* dev_ptr);
+LLMC_API int llmc_ipc_free(void* dev_ptr);
+LLMC_API size_t llmc_ar_region_bytes(int world, int rows_cap, int hidden, int dtype,
+                                     size_t* flag_bytes);
+LLMC_API int llmc_allreduce_add_rmsnorm(const void* partial, void* const* recv_ptrs,
+                                        int32_t* const* flag_ptrs, int32_t* epoch, void* x,
+                                        const void* weight, void* out, int32_t* status,
+                                        int rank, int world, int rows, int rows_cap,
+                                        int hidden, float eps, int dtype,
+                                        llmc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

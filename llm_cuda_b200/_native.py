@@ -48,6 +48,13 @@ SIGNATURES = {
     "llmc_add_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _I, _P]),
     "llmc_swiglu": (_I, [_P, _P, _I, _I, _I, _P]),
     "llmc_argmax_workspace_bytes": (_SZ, [_I]),
+    "llmc_ipc_handle_bytes": (_SZ, []),
+    "llmc_ipc_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
+    "llmc_ipc_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "llmc_ipc_close": (_I, [_P]),
+    "llmc_ipc_free": (_I, [_P]),
+    "llmc_ar_region_bytes": (_SZ, [_I, _I, _I, _I, ctypes.POINTER(_SZ)]),
+    "llmc_allreduce_add_rmsnorm": (_I, [_P] * 8 + [_I] * 5 + [_F, _I, _P]),
     "llmc_argmax": (_I, [_P, _P, _I, _I, _I, _P, _P]),
     "llmc_last_error_string": (ctypes.c_char_p, []),
     "llmc_version": (ctypes.c_char_p, []),

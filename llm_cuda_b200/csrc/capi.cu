@@ -3,6 +3,7 @@
 // Host-side argument validation happens here, before any launch; errors are
 // reported as negative return codes plus a per-thread message, never by
 // throwing across the ABI.
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -42,6 +43,24 @@ cudaError_t launch_swiglu(const void* gu, void* out, int rows, int inter, int dt
                           cudaStream_t stream);
 cudaError_t launch_argmax(const void* x, int64_t* out, int rows, int n, int dtype,
                           unsigned long long* keys, int* counters, int sms, cudaStream_t stream);
+namespace ar {
+struct Params {
+  const void* partial;
+  void* const* recv;
+  int32_t* const* flags;
+  int32_t* epoch;
+  void* x;
+  const void* w;
+  void* h;
+  int32_t* status;
+  int rank, world, rows, rows_cap, hidden;
+  float eps;
+};
+}  // namespace ar
+size_t ar_recv_bytes(int world, int rows_cap, int hidden, int elem);
+size_t ar_flag_bytes(int world, int rows_cap);
+cudaError_t launch_allreduce_add_rmsnorm(const ar::Params& p, int dtype, std::string* err,
+                                         cudaStream_t stream);
 }  // namespace llmc
 
 namespace {
@@ -340,6 +359,86 @@ int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype, void* w
   cudaError_t e = llmc::launch_argmax(x, out, rows, n, dtype, keys, counters,
                                       llmc::balanced_grid(), (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_fail(e, "llmc_argmax");
+  return LLMC_OK;
+}
+
+size_t llmc_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int llmc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle) {
+  g_last_error.clear();
+  if (!dev_ptr || !handle || bytes == 0) return fail(LLMC_EINVAL, "llmc_ipc_alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_ipc_alloc: cudaMalloc");
+  e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "llmc_ipc_alloc");
+  }
+  *dev_ptr = p;
+  return LLMC_OK;
+}
+
+int llmc_ipc_open(const void* handle, void** dev_ptr) {
+  g_last_error.clear();
+  if (!handle || !dev_ptr) return fail(LLMC_EINVAL, "llmc_ipc_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_ipc_open");
+  return LLMC_OK;
+}
+
+int llmc_ipc_close(void* dev_ptr) {
+  g_last_error.clear();
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_ipc_close");
+  return LLMC_OK;
+}
+
+int llmc_ipc_free(void* dev_ptr) {
+  g_last_error.clear();
+  cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_ipc_free");
+  return LLMC_OK;
+}
+
+size_t llmc_ar_region_bytes(int world, int rows_cap, int hidden, int dtype, size_t* flag_bytes) {
+  if (world <= 0 || rows_cap <= 0 || hidden <= 0 || !valid_dtype(dtype)) {
+    if (flag_bytes) *flag_bytes = 0;
+    return 0;
+  }
+  if (flag_bytes) *flag_bytes = llmc::ar_flag_bytes(world, rows_cap);
+  return llmc::ar_recv_bytes(world, rows_cap, hidden, dtype == LLMC_F32 ? 4 : 2);
+}
+
+int llmc_allreduce_add_rmsnorm(const void* partial, void* const* recv_ptrs,
+                               int32_t* const* flag_ptrs, int32_t* epoch, void* x,
+                               const void* weight, void* out, int32_t* status, int rank,
+                               int world, int rows, int rows_cap, int hidden, float eps,
+                               int dtype, llmc_stream_t stream) {
+  g_last_error.clear();
+  if (!valid_dtype(dtype)) return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: unknown dtype");
+  if (world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: need 0 <= rank < world <= 8");
+  if (rows < 0 || rows > rows_cap || hidden <= 0)
+    return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: need 0 <= rows <= rows_cap, hidden > 0");
+  if (!partial || !recv_ptrs || !flag_ptrs || !epoch || !x || !weight || !out || !status)
+    return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: NULL pointer argument");
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al(partial) || !al(x) || !al(weight) || !al(out))
+    return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: tensors must be 16-byte aligned");
+  if (rows == 0) return LLMC_OK;
+  llmc::ar::Params p;
+  p.partial = partial; p.recv = recv_ptrs; p.flags = flag_ptrs; p.epoch = epoch;
+  p.x = x; p.w = weight; p.h = out; p.status = status;
+  p.rank = rank; p.world = world; p.rows = rows; p.rows_cap = rows_cap; p.hidden = hidden;
+  p.eps = eps;
+  std::string err;
+  cudaError_t e = llmc::launch_allreduce_add_rmsnorm(p, dtype, &err, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_fail(e, "llmc_allreduce_add_rmsnorm", err);
   return LLMC_OK;
 }
 

@@ -61,10 +61,16 @@ class DecodeConfig:
 
 
 class TensorParallel:
-    """Rank/size of the TP group and its all-reduce (identity when size == 1)."""
+    """Rank/size of the TP group and its all-reduce (identity when size == 1).
+
+    ``fused`` (an ``NvlinkAllReduce``, set by ``Llama3DecodeModel.enable_fused_allreduce``)
+    takes the decode rows' all-reduce + residual add + RMSNorm in one kernel; rows it
+    does not take (prefill) use ``all_reduce_`` (NCCL).
+    """
 
     def __init__(self, rank: int = 0, size: int = 1, group=None):
         self.rank, self.size, self.group = rank, size, group
+        self.fused = None
 
     def all_reduce_(self, x: torch.Tensor) -> torch.Tensor:
         if self.size > 1:
@@ -220,7 +226,7 @@ class Llama3DecodeModel:
         else:
             gate, up = gu.split(self.inter, dim=-1)
             h = (gate * torch.sigmoid(gate)) * up         # swiglu.py:103-107
-        return self.tp.all_reduce_(self._linear(h, L["wdown"], "down"))
+        return self._linear(h, L["wdown"], "down")   # row-parallel partial
 
     def _linear(self, x: torch.Tensor, w: torch.Tensor, name: str) -> torch.Tensor:
         """``x @ w.T`` for the projection ``name``: the tcgen05 decode GEMM when ``name``
@@ -240,6 +246,26 @@ class Llama3DecodeModel:
                 and self.lm_head.shape[0] % 128 == 0 and h.shape[-1] % 64 == 0):
             return decode_gemm(h, self.lm_head)
         return F.linear(h, self.lm_head)
+
+    def enable_fused_allreduce(self, rows_cap: int) -> None:
+        """Serve the all-reduce + residual add + RMSNorm of up to ``rows_cap`` decode
+        rows with the one-shot NVLink kernel (every rank of the group must call it)."""
+        from ...kernels.allreduce import NvlinkAllReduce
+
+        if self.tp.size > 1 and self.tp.fused is None:
+            self.tp.fused = NvlinkAllReduce(self.tp.group, self.tp.rank, self.tp.size, rows_cap,
+                                            self.cfg.hidden_size, self.dtype, self.device)
+
+    def _reduce_add_norm(self, x: torch.Tensor, w: torch.Tensor, partial: torch.Tensor | None):
+        """All-reduce of a row-parallel ``partial`` (tensor_parallel.py:83-90), residual
+        add and RMSNorm: returns ``(x, h)``.  The fused NVLink kernel takes it when
+        enabled and the rows fit; otherwise NCCL + the add/norm kernel."""
+        if partial is None:
+            return self._add_norm(x, w, None)
+        f = self.tp.fused
+        if f is not None and f.supports(x) and x.is_contiguous():
+            return x, f.add_rmsnorm(partial.contiguous(), x, w, self.cfg.rms_norm_eps)
+        return self._add_norm(x, w, self.tp.all_reduce_(partial))
 
     def _add_norm(self, x: torch.Tensor, w: torch.Tensor, delta: torch.Tensor | None):
         """Residual add (model.py:37,42) + RMSNorm (norm.py:31-33): returns ``(x, h)``.
@@ -263,7 +289,7 @@ class Llama3DecodeModel:
         delta = None
         for li, L in enumerate(self.layers):
             lc = cache.get_layer(li)
-            x, h = self._add_norm(x, L["in_norm"], delta)
+            x, h = self._reduce_add_norm(x, L["in_norm"], delta)
             q, k, v = self._split_qkv(F.linear(h, L["wqkv"]), B, S)
             q_rot = lc.append_rotary(q, k, v, self.rope)
             kc, vc = lc.get_kv()                             # rotated k as stored
@@ -272,10 +298,9 @@ class Llama3DecodeModel:
                 q_rot, kc.repeat_interleave(rep, dim=1), vc.repeat_interleave(rep, dim=1),
                 is_causal=True)
             attn = attn.transpose(1, 2).reshape(B, S, self.hq * cfg.head_dim)
-            o = self.tp.all_reduce_(F.linear(attn, L["wo"]))
-            x, h = self._add_norm(x, L["post_norm"], o)
+            x, h = self._reduce_add_norm(x, L["post_norm"], F.linear(attn, L["wo"]))
             delta = self._mlp(L, h)
-        x, h = self._add_norm(x, self.final_norm, delta)
+        x, h = self._reduce_add_norm(x, self.final_norm, delta)
         return F.linear(h[:, -1], self.lm_head)
 
     def decode_step(self, ids: torch.Tensor, cache: PagedKVCache,
@@ -287,7 +312,7 @@ class Llama3DecodeModel:
         delta = None
         for li, L in enumerate(self.layers):
             lc = cache.get_layer(li)
-            x, h = self._add_norm(x, L["in_norm"], delta)
+            x, h = self._reduce_add_norm(x, L["in_norm"], delta)
             q, k, v = self._split_qkv(self._linear(h, L["wqkv"], "qkv"), B, 1)
             if self.attn_core is not None:
                 attn = self.attn_core(li, q, k, v, lc)
@@ -296,10 +321,9 @@ class Llama3DecodeModel:
                 attn = lc.rope_append_decode(q, k, v, self.rope,
                                              partition_tokens=partition_tokens)
             attn = attn.reshape(B, 1, self.hq * cfg.head_dim)
-            o = self.tp.all_reduce_(self._linear(attn, L["wo"], "o"))
-            x, h = self._add_norm(x, L["post_norm"], o)
+            x, h = self._reduce_add_norm(x, L["post_norm"], self._linear(attn, L["wo"], "o"))
             delta = self._mlp(L, h)
-        x, h = self._add_norm(x, self.final_norm, delta)
+        x, h = self._reduce_add_norm(x, self.final_norm, delta)
         return self._lm_head(h[:, 0])
 
     def bytes_per_step(self, cache: PagedKVCache) -> tuple[int, int]:
