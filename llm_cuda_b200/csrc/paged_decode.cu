@@ -166,12 +166,13 @@ struct Walker {
   int B, Hkv, HG, T, cap, total_items;
   bool balanced;
   int i, phase;
-  long long x, start, end, p0, phase_end;
+  // Chunk positions in the flattened row space; the host keeps the total below 2^31.
+  int x, start, end, p0, phase_end;
 
   // Sequence b of flattened chunk x and the first chunk of x's row.
-  __device__ void locate(long long xx, int& b, long long& row_begin) const {
+  __device__ void locate(int xx, int& b, int& row_begin) const {
     const int RS = Hkv * HG;
-    const long long key = xx / RS;       // prefix[b] * RS <= xx  <=>  prefix[b] <= xx / RS
+    const int key = xx / RS;             // prefix[b] * RS <= xx  <=>  prefix[b] <= xx / RS
     int lo = 0, hi = B;
     while (hi - lo > 1) {
       const int mid = (lo + hi) >> 1;
@@ -179,7 +180,7 @@ struct Walker {
     }
     b = lo;
     const int n = prefix[b + 1] - prefix[b];
-    const long long local = xx - (long long)prefix[b] * RS;
+    const int local = xx - prefix[b] * RS;
     row_begin = xx - local % n;
   }
 
@@ -189,16 +190,15 @@ struct Walker {
     total_items = prefix[B];
     i = blockIdx.x;
     const long long total = (long long)prefix[B] * Hkv * HG;
-    start = (long long)blockIdx.x * total / gridDim.x;
-    end = ((long long)blockIdx.x + 1) * total / gridDim.x;
+    start = (int)((long long)blockIdx.x * total / gridDim.x);
+    end = (int)(((long long)blockIdx.x + 1) * total / gridDim.x);
     // The range's last segment (usually the head of a row that the next CTA
     // continues) goes first, then the range from its start: both segments a CTA
     // shares with its neighbours finish early, so the row merges they trigger run
     // while the other CTAs are still streaming rather than at the end.
     p0 = start;
     if (balanced && end > start) {
-      int b;
-      long long rb;
+      int b, rb;
       locate(end - 1, b, rb);
       p0 = rb > start ? rb : start;
     }
@@ -227,14 +227,13 @@ struct Walker {
       phase_end = p0;
     }
     const int RS = Hkv * HG;
-    int b;
-    long long row_begin;
+    int b, row_begin;
     locate(x, b, row_begin);
     const int n = prefix[b + 1] - prefix[b];
-    const int ri = (int)((row_begin - (long long)prefix[b] * RS) / n);
-    const int c0 = (int)(x - row_begin);
-    const long long row_end = row_begin + n;
-    long long e = phase_end < row_end ? phase_end : row_end;
+    const int ri = (row_begin - prefix[b] * RS) / n;
+    const int c0 = x - row_begin;
+    const int row_end = row_begin + n;
+    int e = phase_end < row_end ? phase_end : row_end;
     if (e > x + cap) e = x + cap;
     pc.b = b; pc.kvh = ri / HG; pc.hg = ri - pc.kvh * HG;
     pc.L = lens[b];
@@ -283,6 +282,38 @@ __device__ __forceinline__ void merge_row(const Params& p, const Piece& it, int 
   const int hq = it.kvh * p.G + it.hg * 8 + hn;
   T* orow = reinterpret_cast<T*>(p.out) + ((size_t)it.b * p.Hq + hq) * D + dq;
   constexpr int U = 4;                       // segments whose loads are issued together
+  if (D <= 128 && it.cl - it.cf < U) {
+    // At most 4 CTAs hold the row (the usual case): every log2-sum-exp and every
+    // partial value of this lane is requested at once, one L2 round trip in all.
+    constexpr int DL = D / 4;
+    float l[U], v[U][DL];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool ok = live(it.cf + u);
+      l[u] = ok ? __ldcg(lse + (size_t)(it.cf + u) * 8) : -INFINITY;
+      const float* po = pobase + (size_t)(it.cf + u) * 8 * D;
+#pragma unroll
+      for (int j = 0; j < DL; ++j) v[u][j] = ok ? __ldcg(po + 4 * j) : 0.f;
+    }
+    float M = l[0];
+#pragma unroll
+    for (int u = 1; u < U; ++u) M = fmaxf(M, l[u]);
+    float w[U], S = 0.f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      w[u] = exp2f(l[u] - M);
+      S += w[u];
+    }
+    const float inv = 1.f / S;
+#pragma unroll
+    for (int j = 0; j < DL; ++j) {
+      float a = 0.f;
+#pragma unroll
+      for (int u = 0; u < U; ++u) a = fmaf(w[u], v[u][j], a);
+      orow[4 * j] = from_f32<T>(a * inv);
+    }
+    return;
+  }
   constexpr int DPL = D / 4;                 // head_dim values of this lane: dq + 4j
   constexpr int CH = DPL < 16 ? DPL : 16;    // accumulated per pass
   // Online max / sum over the segments' log2-sum-exps, U loads in flight at a time.
@@ -386,6 +417,23 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   if (warp == kConsumers && lane == 0) {
     prefetch_tensormap(&tmap_k);
     prefetch_tensormap(&tmap_v);
+  }
+  if (warp == kConsumers && lane == 1) {
+    // The block table is read right after the length scan; by then the previous
+    // step's K/V stream has evicted it from L2.  Each CTA asks L2 for its share now,
+    // overlapping the previous kernel (a hint only: the reads that matter come after
+    // griddepcontrol.wait, and L2 is coherent with any write to the table before it).
+    const uintptr_t base = reinterpret_cast<uintptr_t>(p.block_table);
+    const size_t bytes = (size_t)p.B * p.max_pages * sizeof(int32_t);
+    const size_t per = ((bytes + gridDim.x - 1) / gridDim.x + 15) & ~(size_t)15;
+    const size_t off = per * blockIdx.x;
+    if ((base & 15) == 0 && off < bytes) {
+      const size_t n = (bytes - off < per ? bytes - off : per) & ~(size_t)15;
+      if (n)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off),
+                     "r"((uint32_t)n)
+                     : "memory");
+    }
   }
   // Everything above overlaps the previous kernel under programmatic dependent
   // launch; lengths, block table and pages are read only after this wait.
@@ -1325,6 +1373,12 @@ int balanced_grid() { return device_info().sms; }
 
 // Work split of the fast kernel: uniform partitions of Tpart tokens, or (Tpart == 0)
 // the balanced split, whose counters head the part_lse buffer.
+// The balanced split keeps chunk positions in 32 bits: every row's chunks together.
+static bool balanced_fits(int B, int Hkv, int HG, int max_pages, int P) {
+  const long long chunks = ((long long)max_pages * P + fast::kStageTok - 1) / fast::kStageTok;
+  return (long long)B * Hkv * HG * chunks < (1ll << 31) - 1;
+}
+
 static void set_split(fast::Params& p, int Tpart, float* part_o, float* part_lse) {
   p.part_o = part_o;
   if (Tpart == 0) {
@@ -1372,6 +1426,8 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
   if (B == 0) return cudaSuccess;
   if (!fast_path_applies(dtype, D, P, max_pages, Tpart, B, q_raw, kp, vp))
     return cudaErrorNotSupported;
+  if (Tpart == 0 && !balanced_fits(B, Hkv, (Hq / Hkv + 7) / 8, max_pages, P))
+    return cudaErrorNotSupported;
   const int G = Hq / Hkv;
   fast::Params p;
   p.q = q_raw; p.out = out; p.block_table = bt;
@@ -1400,7 +1456,8 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
   const int G = Hq / Hkv;
   if (B == 0) return cudaSuccess;
   const bool fast_ok = !(flags & LLMC_DECODE_FORCE_GENERIC) &&
-                       fast_path_applies(dtype, D, P, max_pages, Tpart, B, q, kp, vp);
+                       fast_path_applies(dtype, D, P, max_pages, Tpart, B, q, kp, vp) &&
+                       (Tpart > 0 || balanced_fits(B, Hkv, (G + 7) / 8, max_pages, P));
   if (Tpart == 0 && !fast_ok) {
     *err = "the balanced split (partition_tokens 0) needs the TMA kernel's shapes";
     return cudaErrorNotSupported;
