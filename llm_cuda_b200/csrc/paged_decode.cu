@@ -1,26 +1,35 @@
 // Paged GQA flash-decode for sm_100a + the split-K log-sum-exp merge.
 //
-// Work item = (sequence b, partition of `T` tokens, KV head, group of <= 8 query
-// heads).  All query heads of a KV head (the GQA group) sit in one CTA, so every
-// K/V byte is read from HBM once per step.
+// Row = (sequence b, KV head, group of <= 8 query heads).  All query heads of a KV
+// head (the GQA group) sit in one CTA, so every K/V byte is read from HBM once per
+// step.
 //
-// Fast kernel (bf16/fp16, head_dim 64/128/256): persistent, one CTA per SM,
-// walking work items round-robin.  The last warp is the producer: it reads the block
-// table and issues TMA (cp.async.bulk.tensor.2d, 128-byte swizzle) loads of the
-// K and V page rows of each 64-token stage into a ring of shared-memory slots,
-// signalling per-slot "full" mbarriers with transaction bytes.  Warps 0-2 are
-// consumers: stage s is processed by warp s % 3, which
-//   S^T[16 tok x 8 heads] = K[16 x d] . Q^T      (mma.sync m16n8k16, K via ldmatrix)
-//   online softmax per head in the log2 domain   (warp shuffles across the 8 rows)
-//   O^T[d x 8 heads]     += V^T[d x 16] . P^T    (V via ldmatrix.trans, P via movmatrix)
-// and releases the slot on its "empty" mbarrier.  At the end of an item the three
-// consumers combine (m, l, O) through shared memory and write either the final
-// output (single-partition sequence) or a normalised partial + log2-sum-exp.
+// Fast kernel (bf16/fp16, head_dim 64/128/256): persistent, one CTA per SM, 8 warps.
+//  * Work split.  Balanced (partition_tokens 0, the default): the 64-token chunks of
+//    all rows are laid end to end and CTA c streams chunks [c*total/G, (c+1)*total/G),
+//    in pieces of <= 2048 tokens; the part of a row inside one CTA is a segment.
+//    Uniform (partition_tokens T): items (row, partition of T tokens) round-robin.
+//  * Warp 6, the producer, reads the block table and issues TMA (cp.async.bulk.tensor,
+//    128-byte swizzle) loads of the K and V page rows of each stage into a ring of
+//    shared-memory slots, signalling per-slot "full" mbarriers with transaction bytes.
+//  * Warps 0-5, the consumers, in 3 groups of 2: stage s goes to group s % 3, each
+//    warp of the group taking half of the stage's 16-token tiles:
+//      S^T[16 tok x 8 heads] = K[16 x d] . Q^T      (mma.sync m16n8k16, K via ldmatrix)
+//      online softmax per head in the log2 domain   (warp shuffles across the 8 rows)
+//      O^T[d x 8 heads]     += V^T[d x 16] . P^T    (V via ldmatrix.trans, P via movmatrix)
+//    then release the slot on its "empty" mbarrier.  At a segment's end the last
+//    consumer warp combines the six (m, l, O) through shared memory and writes the
+//    output (whole row), a partial + log2-sum-exp (uniform split), or hands the
+//    partial to the merge warp (balanced split).
+//  * Warp 7, the merge warp (balanced split): publishes handed-off partials, and the
+//    CTA that completes a row merges it in place; it also zeroes empty rows and, in
+//    the fused step, publishes the grown lengths.
+//  * FUSE: RoPE of the new token's q/k and its page append happen in the same pass.
 //
 // Generic kernel (any dtype incl. fp32, any head_dim <= 256, any page size):
-// one CTA per item, SIMT dot products, exact expf; same partial format.
+// one CTA per item, SIMT dot products, exact expf; uniform partial format.
 //
-// Merge kernel: out = sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M).
+// Merge kernel (uniform split): out = sum_i 2^(lse_i - M) o_i / sum_i 2^(lse_i - M).
 #include <math.h>
 
 #include <string>
@@ -147,14 +156,30 @@ struct Piece {
   // Balanced, last piece of a split row's segment: CTAs cf..cl hold the row (nlive
   // of them own chunks); total = chunks of all rows.
   int cf, cl, nlive;
-  long long total;
+  int total;
 };
 
-// CTA owning chunk x when `total` chunks are cut into G equal ranges
-// [c*total/G, (c+1)*total/G): the largest c with c*total/G <= x.
-__device__ __forceinline__ int chunk_owner(long long x, long long total, int G) {
-  return (int)(((x + 1) * G + total - 1) / total) - 1;
-}
+// The split of `total` chunks (< 2^31) into G ranges [start(c), start(c+1)) with
+// start(c) = floor(c * total / G), in 32-bit arithmetic: with total = q*G + r,
+// start(c) = c*q + floor(c*r / G) exactly (c*q < 2^31, c*r < G^2).  64-bit integer
+// division is a long software routine on the GPU; this runs in a few instructions.
+struct ChunkSplit {
+  int q, r, G, total;
+  __device__ __forceinline__ void init(int total_, int G_) {
+    total = total_; G = G_; q = total_ / G_; r = total_ - q * G_;
+  }
+  __device__ __forceinline__ int start(int c) const { return c * q + (c * r) / G; }
+  // CTA owning chunk x (0 <= x < total): the largest c with start(c) <= x.  A float
+  // estimate is within one of it; the exact starts settle the rest.
+  __device__ __forceinline__ int owner(int x) const {
+    int c = (int)((float)x * (float)G / (float)total);
+    c = c < 0 ? 0 : (c >= G ? G - 1 : c);
+    while (c + 1 < G && start(c + 1) <= x) ++c;
+    while (c > 0 && start(c) > x) --c;
+    return c;
+  }
+  __device__ __forceinline__ bool live(int c) const { return start(c) != start(c + 1); }
+};
 
 // The sequence of pieces of this CTA.  Uniform mode: items blockIdx.x, +gridDim.x,
 // ... (one piece each).  Balanced mode: a walk over chunks [start, end) of the
@@ -168,6 +193,7 @@ struct Walker {
   int i, phase;
   // Chunk positions in the flattened row space; the host keeps the total below 2^31.
   int x, start, end, p0, phase_end;
+  ChunkSplit split;
 
   // Sequence b of flattened chunk x and the first chunk of x's row.
   __device__ void locate(int xx, int& b, int& row_begin) const {
@@ -189,9 +215,9 @@ struct Walker {
     balanced = p.balanced != 0;
     total_items = prefix[B];
     i = blockIdx.x;
-    const long long total = (long long)prefix[B] * Hkv * HG;
-    start = (int)((long long)blockIdx.x * total / gridDim.x);
-    end = (int)(((long long)blockIdx.x + 1) * total / gridDim.x);
+    split.init(prefix[B] * Hkv * HG, gridDim.x);
+    start = split.start(blockIdx.x);
+    end = split.start(blockIdx.x + 1);
     // The range's last segment (usually the head of a row that the next CTA
     // continues) goes first, then the range from its start: both segments a CTA
     // shares with its neighbours finish early, so the row merges they trigger run
@@ -246,16 +272,13 @@ struct Walker {
     pc.cf = pc.cl = pc.nlive = 0;
     pc.total = 0;
     if (!pc.whole && pc.last) {   // only the segment epilogue needs them
-      const long long total = (long long)prefix[B] * RS;
-      const int G = gridDim.x;
-      pc.total = total;
-      pc.cf = chunk_owner(row_begin, total, G);
-      pc.cl = chunk_owner(row_end - 1, total, G);
-      if (total >= G) {
+      pc.total = split.total;
+      pc.cf = split.owner(row_begin);
+      pc.cl = split.owner(row_end - 1);
+      if (split.total >= split.G) {
         pc.nlive = pc.cl - pc.cf + 1;
       } else {   // some CTAs own no chunk and hold no segment
-        for (int c = pc.cf; c <= pc.cl; ++c)
-          pc.nlive += ((long long)c * total / G != ((long long)c + 1) * total / G);
+        for (int c = pc.cf; c <= pc.cl; ++c) pc.nlive += split.live(c);
       }
     }
     x = e;
@@ -272,11 +295,9 @@ __device__ __forceinline__ void merge_row(const Params& p, const Piece& it, int 
                                           int nh) {
   if (hn >= nh) return;
   const int G = gridDim.x;
-  const long long total = it.total;
-  auto live = [&](int cc) -> bool {
-    return cc <= it.cl &&
-           (total >= G || (long long)cc * total / G != ((long long)cc + 1) * total / G);
-  };
+  ChunkSplit split;
+  split.init(it.total, G);
+  auto live = [&](int cc) -> bool { return cc <= it.cl && (it.total >= G || split.live(cc)); };
   const float* lse = p.part_lse + (size_t)r * 8 + hn;
   const float* pobase = p.part_o + ((size_t)r * 8 + hn) * D + dq;
   const int hq = it.kvh * p.G + it.hg * 8 + hn;
