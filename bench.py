@@ -702,6 +702,37 @@ def run_c5(args):
         os._exit(0)
 
 
+def run_gemm(args):
+    """--gemm N,K: the tcgen05 decode GEMM y[64, N] = x[64, K] W[N, K]^T alone, on W
+    copies rotating over >= 300 MB (no launch finds its weights in L2); one JSON line
+    with the weight-streaming rate.  Used for the decode-GEMM profiles."""
+    from llm_cuda_b200 import _native as N
+    from llm_cuda_b200.kernels.step_ops import decode_gemm
+
+    N.load()
+    n_out, k = (int(v) for v in args.gemm.split(","))
+    dev = torch.device("cuda", 0)
+    nw = max(2, -(-300_000_000 // (n_out * k * 2)))
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn(64, k, device=dev, generator=g).bfloat16()
+    ws = [(0.02 * torch.randn(n_out, k, device=dev, generator=g)).bfloat16() for _ in range(nw)]
+    for i in range(max(3, args.warmup)):
+        y = decode_gemm(x, ws[i % nw])
+    torch.cuda.synchronize()
+    err = (y.float() - x.float() @ ws[(max(3, args.warmup) - 1) % nw].float().T).abs().max().item()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        decode_gemm(x, ws[i % nw])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"metric": "decode GEMM weight GB/s", "value": n_out * k * 2 / ms / 1e6,
+                      "unit": "GB/s", "ms_per_call": ms, "steps": args.steps,
+                      "config": {"N": n_out, "K": k, "Mb": 64, "weight_copies": nw},
+                      "max_abs_err_vs_fp32": err}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -722,7 +753,12 @@ def main():
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak",
                     help="N>1: weak = N x the config's batch, head-sharded (per-GPU work "
                          "fixed); strong = the config's batch split over N GPUs")
+    ap.add_argument("--gemm", default=None, metavar="N,K",
+                    help="time the tcgen05 decode GEMM alone at Mb=64 (profiling aid)")
     args = ap.parse_args()
+    if args.gemm:
+        run_gemm(args)
+        return
     if args.workload == "c5":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "config 5 reference arm not "
