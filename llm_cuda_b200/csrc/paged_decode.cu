@@ -494,7 +494,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
       prefix[b] = run;
       const int L = eff_len(b, false);
       lens[b] = L;
-      if (FUSE && blockIdx.x == 0) p.lens_next[b] = L;
+      if (FUSE && !p.balanced && blockIdx.x == 0) p.lens_next[b] = L;   // for the merge launch
       run += units(L);
     }
     if (lane == 31) prefix[p.B] = incl;

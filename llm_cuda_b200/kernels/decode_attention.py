@@ -114,6 +114,7 @@ class DecodeWorkspace:
         self.part_o = torch.empty(0, dtype=torch.float32, device=device)
         self.part_lse = torch.empty(0, dtype=torch.float32, device=device)
         self._counter_words = None
+        self._balanced_sizes: dict = {}
 
     def lens_next(self, B: int) -> torch.Tensor:
         """int32 [B] scratch for the fused step's advanced lengths."""
@@ -129,11 +130,14 @@ class DecodeWorkspace:
         before a call; the kernel returns them to zero.  They are zeroed here when the
         buffer is new or the row count (hence the counter area) changes.
         """
-        lib = N.load()
-        lse_b = N.ctypes.c_size_t(0)
-        with torch.cuda.device(self.device):
-            o_b = lib.llmc_balanced_partials_bytes(B, Hq, Hkv, d, N.ctypes.byref(lse_b))
-        no, nl = o_b // 4, lse_b.value // 4
+        key = (B, Hq, Hkv, d)
+        sizes = self._balanced_sizes.get(key)
+        if sizes is None:   # one ctypes query per shape, not per call
+            lse_b = N.ctypes.c_size_t(0)
+            with torch.cuda.device(self.device):
+                o_b = N.load().llmc_balanced_partials_bytes(B, Hq, Hkv, d, N.ctypes.byref(lse_b))
+            sizes = self._balanced_sizes[key] = (o_b // 4, lse_b.value // 4)
+        no, nl = sizes
         if self.part_o.numel() < no:
             self.part_o = torch.empty(no, dtype=torch.float32, device=self.device)
         if self.part_lse.numel() < nl:

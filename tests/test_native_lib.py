@@ -93,3 +93,37 @@ def test_missing_library_fails_loudly(monkeypatch):
     monkeypatch.setattr(N, "_LIB_PATH", "/nonexistent/libllmcuda_b200.so")
     with pytest.raises(N.NativeLibraryError):
         N.load()
+
+
+def test_host_validation_of_step_entry_points():
+    """The config-5 step entry points reject bad arguments before touching CUDA."""
+    lib = N.load()
+    nul = None
+    # fused all-reduce: world out of range, rank >= world, rows > rows_cap
+    rc = lib.llmc_allreduce_add_rmsnorm(1, 1, 1, 1, 1, 1, 1, 1, 0, 9, 64, 64, 4096, 1e-5,
+                                        N.LLMC_BF16, nul)
+    assert rc == -1 and b"world" in lib.llmc_last_error_string()
+    rc = lib.llmc_allreduce_add_rmsnorm(1, 1, 1, 1, 1, 1, 1, 1, 2, 2, 64, 64, 4096, 1e-5,
+                                        N.LLMC_BF16, nul)
+    assert rc == -1
+    rc = lib.llmc_allreduce_add_rmsnorm(1, 1, 1, 1, 1, 1, 1, 1, 0, 2, 65, 64, 4096, 1e-5,
+                                        N.LLMC_BF16, nul)
+    assert rc == -1 and b"rows_cap" in lib.llmc_last_error_string()
+    # misaligned tensors
+    rc = lib.llmc_allreduce_add_rmsnorm(18, 16, 16, 16, 16, 16, 16, 16, 0, 2, 8, 64, 4096,
+                                        1e-5, N.LLMC_BF16, nul)
+    assert rc == -1 and b"aligned" in lib.llmc_last_error_string()
+    fb = ctypes.c_size_t(0)
+    assert lib.llmc_ar_region_bytes(2, 64, 4096, N.LLMC_BF16, ctypes.byref(fb)) == 2 * 2 * 64 * 4096 * 2
+    assert fb.value == 2 * 2 * 64 * 4
+    # argmax
+    assert lib.llmc_argmax(1, 1, 70000, 10, N.LLMC_BF16, 8, nul) == -1
+    assert lib.llmc_argmax(1, 1, 4, 10, N.LLMC_BF16, 4, nul) == -1        # misaligned workspace
+    assert lib.llmc_argmax_workspace_bytes(64) == 64 * 12
+    # strided fused step: a sequence stride smaller than the dense one
+    args = [1] * 10 + [128] + [1] * 5 + [4, 32, 8, 128, 16, 16, 1024, 0]
+    rc = lib.llmc_rope_append_decode_strided(*args, 0.1, N.LLMC_BF16, 32 * 128 - 1, 8 * 128, nul)
+    assert rc == -1 and b"stride" in lib.llmc_last_error_string()
+    # decode GEMM shapes
+    assert lib.llmc_decode_gemm(1, 1, 1, 1, 4, 1, 64, 100, 64, 1, nul) == -2
+    assert lib.llmc_decode_gemm_workspace_bytes(300, 128, 64) == 0
