@@ -112,7 +112,8 @@ LLMC_API int llmc_num_partitions(int max_tokens, int partition_tokens);
  *    leaves them at zero.
  *  - llmc_paged_decode returns LLMC_EUNSUPPORTED where the TMA kernel does not apply
  *    (see llmc_decode_balanced_supported). llmc_rope_append_decode then falls back to
- *    uniform partitions that fit the same buffers.
+ *    uniform partitions that fit the same buffers; their log-sum-exps are stored after
+ *    the counter words, which stay zero.
  */
 #define LLMC_PARTITION_BALANCED 0
 
@@ -228,7 +229,9 @@ LLMC_API int llmc_lse_merge(const float* part_o, const float* part_lse, const in
  * (B * Hq * max_parts * (d + 1) * 4 bytes) return LLMC_EINVAL.  The first call on a
  * device looks up the array's address; make it before any stream capture.  All calls
  * share the array, so calls that overlap on the GPU race: issue them in order on one
- * stream.  Arguments as llmc_paged_decode, minus part_o/part_lse/flags.
+ * stream.  Arguments as llmc_paged_decode, minus part_o/part_lse/flags, except that
+ * partition_tokens must be a positive multiple of 64: the balanced split
+ * (LLMC_PARTITION_BALANCED) is not offered here and is rejected with LLMC_EINVAL.
  */
 LLMC_API int llmc_paged_decode_noalloc(const void* q, const void* k_pages, const void* v_pages,
                                        const int32_t* block_table, const int32_t* seq_lens,
@@ -313,9 +316,9 @@ LLMC_API int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype
  *   x += sum (rounded to the dtype); out = x * rsqrt(mean(x^2) + eps) * weight.
  * One launch, one CTA per row. A row pushes its partial to every rank, publishes its
  * epoch with a system-scope release, and waits, bounded at 2 s, for every rank's
- * row. On timeout LLMC_STATUS_WAIT_TIMEOUT is set and the row is left unchanged; the
- * epochs are then out of step, so rebuild the regions. Calls must be issued in the
- * same order on all ranks.
+ * row. On timeout LLMC_STATUS_WAIT_TIMEOUT is set, the row is left unchanged and the
+ * row's epoch still advances. The ranks' epochs may then be out of step, so stop using
+ * the regions and rebuild them. Calls must be issued in the same order on all ranks.
  */
 LLMC_API size_t llmc_ipc_handle_bytes(void);
 LLMC_API int llmc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);

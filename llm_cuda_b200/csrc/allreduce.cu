@@ -110,7 +110,13 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
     }
   }
   __syncthreads();
-  if (s_fail) return;   // rows stay as they were; the status word reports the timeout
+  if (s_fail) {
+    // Rows stay as they were and the status word reports the timeout.  The epoch still
+    // advances: this rank has already published e to its peers, so reusing e on the
+    // next call would pass the wait on the peers' stale flags of this call.
+    if (threadIdx.x == 0) p.epoch[b] = e;
+    return;
+  }
   // 4. sum in rank order from this rank's recv slot, add the residual, normalise
   const T* rv = reinterpret_cast<const T*>(p.recv[p.rank]) + (size_t)par * slot_stride +
                 (size_t)b * row_elems;

@@ -3,6 +3,7 @@
 // Host-side argument validation happens here, before any launch; errors are
 // reported as negative return codes plus a per-thread message, never by
 // throwing across the ABI.
+#include <climits>
 #include <cstring>
 #include <string>
 
@@ -170,7 +171,10 @@ int llmc_paged_decode(const void* q, const void* k_pages, const void* v_pages,
     return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode: page pool rows exceed 2^31");
   if (!q || !k_pages || !v_pages || !block_table || !seq_lens || !out || !status)
     return fail(LLMC_EINVAL, "llmc_paged_decode: NULL pointer argument");
-  const int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
+  const long long cap_tokens = (long long)max_pages_per_seq * page_size;
+  if (cap_tokens > INT_MAX)
+    return fail(LLMC_EINVAL, "llmc_paged_decode: max_pages_per_seq * page_size exceeds 2^31-1");
+  const int max_parts = llmc_num_partitions((int)cap_tokens, partition_tokens);
   if ((partition_tokens == 0 || max_parts > 1) && (!part_o || !part_lse))
     return fail(LLMC_EINVAL,
                 "llmc_paged_decode: part_o/part_lse are required when a sequence can span "
@@ -231,7 +235,11 @@ int llmc_rope_append_decode_strided(
   if (!q || !k_new || !v_new || !q_rot_out || !k_pages || !v_pages || !block_table || !seq_lens ||
       !cos_tab || !sin_tab || !out || !lens_next || !status)
     return fail(LLMC_EINVAL, "llmc_rope_append_decode: NULL pointer argument");
-  int max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
+  const long long cap_tokens = (long long)max_pages_per_seq * page_size;
+  if (cap_tokens > INT_MAX)
+    return fail(LLMC_EINVAL,
+                "llmc_rope_append_decode: max_pages_per_seq * page_size exceeds 2^31-1");
+  int max_parts = llmc_num_partitions((int)cap_tokens, partition_tokens);
   if ((partition_tokens == 0 || max_parts > 1) && (!part_o || !part_lse))
     return fail(LLMC_EINVAL, "llmc_rope_append_decode: part_o/part_lse are required");
   if (B == 0) return LLMC_OK;
@@ -250,18 +258,23 @@ int llmc_rope_append_decode_strided(
     if (partition_tokens == 0) {
       // The balanced split needs the fused kernel; the SIMT kernel gets uniform
       // partitions, as many as the balanced workspace holds.
+      // The uniform log-sum-exps go after the balanced split's counter words, so the
+      // counters stay zero for a later balanced call on the same buffers.
       size_t lse_b = 0;
       const size_t o_b = llmc_balanced_partials_bytes(B, Hq, Hkv, d, &lse_b);
+      const size_t cw = (size_t)llmc::balanced_counter_words(B * Hkv * ((Hq / Hkv + 7) / 8));
+      const size_t lse_words = lse_b / sizeof(float) > cw ? lse_b / sizeof(float) - cw : 0;
       size_t per_part = 0;
       const size_t o1 = llmc_decode_partials_bytes(B, Hq, d, 1, &per_part);
       size_t fit = o1 ? o_b / o1 : 1;
-      if (per_part && lse_b / per_part < fit) fit = lse_b / per_part;
+      if (per_part && lse_words * sizeof(float) / per_part < fit)
+        fit = lse_words * sizeof(float) / per_part;
       if (fit < 1) fit = 1;
-      const long long cap = (long long)max_pages_per_seq * page_size;
-      long long T = (cap + (long long)fit - 1) / (long long)fit;
+      long long T = (cap_tokens + (long long)fit - 1) / (long long)fit;
       T = (T + 63) / 64 * 64;
       partition_tokens = (int)(T < (1ll << 30) ? T : (1ll << 30));
-      max_parts = llmc_num_partitions((int)cap, partition_tokens);
+      max_parts = llmc_num_partitions((int)cap_tokens, partition_tokens);
+      part_lse += cw;
     }
     int rc = llmc_rope_append(q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens,
                               cos_tab, sin_tab, B, 1, Hq, Hkv, d, page_size, max_pages_per_seq,

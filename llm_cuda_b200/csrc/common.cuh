@@ -246,6 +246,17 @@ __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
   return __float2bfloat16_rn(x);
 }
 
+// Attention score with the reference's torch rounding (attention.py:67 of llm-cuda):
+// torch.matmul(q, k^T) is rounded to the tensor dtype, then "/ sqrt(d)" is computed
+// in fp32 and rounded again.  For fp32 both roundings are the identity.  The division
+// is a multiplication by the fp32 reciprocal here; the two differ only when the fp32
+// quotient lies within one fp32 ulp of a 16-bit rounding boundary.
+template <typename T>
+__device__ __forceinline__ float ref_score(float qk, float scale) {
+  const float a = to_f32(from_f32<T>(qk));
+  return to_f32(from_f32<T>(__fmul_rn(a, scale)));
+}
+
 // One RoPE output element with the reference's torch rounding (rotary.py:104-109):
 // first half  x*cos + (-x_partner)*sin, second half x*cos + x_partner*sin; each
 // product and the sum are rounded to T (no FMA contraction).

@@ -21,6 +21,7 @@
 //    later reads.  Calls whose work overlaps on the GPU (other streams, other
 //    host threads) race on the array; issue them in order on one stream.
 //  * No cudaMalloc, cudaFree or other allocating routine is called.
+#include <climits>
 #include <mutex>
 #include <string>
 
@@ -84,8 +85,12 @@ LLMC_API int llmc_paged_decode_noalloc(const void* q, const void* k_pages, const
   llmc::set_last_error("");
   if (dtype != LLMC_F32 && dtype != LLMC_F16 && dtype != LLMC_BF16)
     return fail(LLMC_EINVAL, "llmc_paged_decode_noalloc: unknown dtype");
+  if (partition_tokens == LLMC_PARTITION_BALANCED)
+    return fail(LLMC_EINVAL,
+                "llmc_paged_decode_noalloc: the balanced split (partition_tokens 0) is not "
+                "supported here; pass a positive multiple of 64");
   if (B < 0 || Hq <= 0 || Hkv <= 0 || d <= 0 || page_size <= 0 || max_pages_per_seq <= 0 ||
-      num_pages <= 0 || partition_tokens <= 0)
+      num_pages <= 0 || partition_tokens < 0)
     return fail(LLMC_EINVAL, "llmc_paged_decode_noalloc: sizes must be positive");
   if (Hq % Hkv) return fail(LLMC_EINVAL, "llmc_paged_decode_noalloc: Hq must be a multiple of Hkv");
   if (d > 256) return fail(LLMC_EUNSUPPORTED, "llmc_paged_decode_noalloc: head_dim > 256");
@@ -99,6 +104,9 @@ LLMC_API int llmc_paged_decode_noalloc(const void* q, const void* k_pages, const
   if (!q || !k_pages || !v_pages || !block_table || !seq_lens || !out || !status)
     return fail(LLMC_EINVAL, "llmc_paged_decode_noalloc: NULL pointer argument");
   const long long cap_tokens = (long long)max_pages_per_seq * page_size;
+  if (cap_tokens > INT_MAX)
+    return fail(LLMC_EINVAL,
+                "llmc_paged_decode_noalloc: max_pages_per_seq * page_size exceeds 2^31-1");
   const int max_parts = (int)((cap_tokens + partition_tokens - 1) / partition_tokens);
   const size_t rows = (size_t)B * Hq * max_parts;
   const size_t need = rows * (size_t)d + rows;

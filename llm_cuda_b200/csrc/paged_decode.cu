@@ -81,6 +81,7 @@ struct Params {
   int B, Hq, Hkv, G, HG, P, max_pages, T, max_parts, num_pages, nstages;
   int max_entries;   // block-table entries one work item can touch (T / P + 2)
   float scale_log2;  // softmax scale * log2(e)
+  float scale;       // softmax scale (scores are rounded as the reference's torch path)
   // Fused RoPE + append (FUSE kernels only).  q holds the RAW query; the new token of
   // sequence b sits at position seq_lens[b] (lengths before the append): its q and k
   // are rotated here with cos/sin row pos, k/v are written to the pages, and the
@@ -900,7 +901,10 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             const int tok = j * 16 + g + ((r >> 1) << 3);
-            const float v = (tok < my_valid) ? sacc[j][r] * p.scale_log2 : -INFINITY;
+            // scores rounded at the reference torch path's points, then log2 domain
+            const float v = (tok < my_valid)
+                                ? ref_score<T>(sacc[j][r], p.scale) * 1.4426950408889634f
+                                : -INFINITY;
             sacc[j][r] = v;
             mloc[r & 1] = fmaxf(mloc[r & 1], v);
           }
@@ -1144,7 +1148,7 @@ paged_decode_simt_kernel(const T* __restrict__ q, const T* __restrict__ k_pages,
         const float* qr = qs + n * D;
         float a = 0.f;
         for (int d = 0; d < D; ++d) a = fmaf(qr[d], to_f32(kr[d]), a);
-        s = a * scale;
+        s = ref_score<T>(a, scale);
       }
       sc[n * kChunk + t] = s;
     }
@@ -1457,7 +1461,7 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
   p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
   p.max_pages = max_pages; p.num_pages = num_pages;
   set_split(p, Tpart, part_o, part_lse);
-  p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
+  p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f; p.scale = scale;
   p.k_new = k_new; p.v_new = v_new; p.cos_tab = cos_tab; p.sin_tab = sin_tab;
   p.k_pages = kp; p.v_pages = vp; p.q_rot_out = q_rot_out; p.lens_next = lens_next;
   p.rope_max_pos = rope_max_pos;
@@ -1483,7 +1487,7 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
     *err = "the balanced split (partition_tokens 0) needs the TMA kernel's shapes";
     return cudaErrorNotSupported;
   }
-  const int max_parts = Tpart > 0 ? (max_pages * P + Tpart - 1) / Tpart : 0;
+  const int max_parts = Tpart > 0 ? (int)(((long long)max_pages * P + Tpart - 1) / Tpart) : 0;
   if (fast_ok) {
     fast::Params p;
     p.q = q; p.out = out; p.block_table = bt;
@@ -1492,7 +1496,7 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
     p.B = B; p.Hq = Hq; p.Hkv = Hkv; p.G = G; p.HG = (G + 7) / 8; p.P = P;
     p.max_pages = max_pages; p.num_pages = num_pages;
     set_split(p, Tpart, part_o, part_lse);
-    p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f;
+    p.nstages = 0; p.scale_log2 = scale * 1.4426950408889634f; p.scale = scale;
     p.k_new = p.v_new = p.cos_tab = p.sin_tab = nullptr;
     p.k_pages = p.v_pages = p.q_rot_out = nullptr;
     p.lens_next = nullptr;

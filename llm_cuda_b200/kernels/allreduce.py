@@ -71,6 +71,7 @@ class NvlinkAllReduce:
         self.flag_ptrs = torch.tensor(flags, dtype=torch.int64, device=self.device)
         self.epoch = torch.zeros(rows_cap, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.failed = False     # set once a wait timeout has been reported
         dist.barrier(group=group)   # every rank has mapped every region before first use
 
     def supports(self, x: torch.Tensor) -> bool:
@@ -81,6 +82,10 @@ class NvlinkAllReduce:
     def add_rmsnorm(self, partial: torch.Tensor, x: torch.Tensor, weight: torch.Tensor,
                     eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
         """``x += all_reduce(partial)`` in place; returns ``rmsnorm(x) * weight``."""
+        if self.failed:
+            raise N.DeviceStatusError(
+                "NvlinkAllReduce: a previous call timed out waiting for a peer; the ranks' "
+                "epochs are out of step, so this instance refuses further calls (rebuild it)")
         if not (x.is_contiguous() and partial.is_contiguous()):
             raise ValueError("x and partial must be contiguous")
         rows = x.numel() // self.hidden
@@ -95,7 +100,13 @@ class NvlinkAllReduce:
         return out
 
     def check_status(self) -> None:
-        N.raise_on_status(self.status)
+        """Synchronise and raise ``DeviceStatusError`` if a call timed out; after that the
+        instance refuses further calls."""
+        try:
+            N.raise_on_status(self.status)
+        except N.DeviceStatusError:
+            self.failed = True
+            raise
 
     def close(self) -> None:
         """Unmap the peers' regions and free this rank's (call after a barrier)."""

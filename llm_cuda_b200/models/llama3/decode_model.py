@@ -3,9 +3,11 @@
 The caller of the decode-attention path: one decode step of a Llama-3 model
 (``src/llm_cuda/models/llama3/model.py:14-107,178-218`` of llm-cuda) with
 
-* the attention hot path on the CUDA kernels of this package — fused RoPE + page
-  append (``llmc_rope_append``) and paged flash-decode + LSE merge — instead of
-  ``build_rope_cache`` / ``apply_rotary`` / ``append`` / ``get_kv`` /
+* the attention hot path as ONE launch per layer: the fused decode kernel
+  (``llmc_rope_append_decode_strided``) rotates the new token's q/k, appends k/v to
+  the pages and attends over the whole context with the balanced split and its
+  in-kernel merge, reading q/k/v in place from the QKV projection output — instead
+  of ``build_rope_cache`` / ``apply_rotary`` / ``append`` / ``get_kv`` /
   ``triton_decode_attention`` (``attention.py:100-150``);
 * tensor parallelism over ranks, one process per GPU.  Shards follow the
   reference's layout (``parallel/tensor_parallel.py:8-90``): q/k/v/gate/up are
@@ -14,9 +16,10 @@ The caller of the decode-attention path: one decode step of a Llama-3 model
   reference's in-process sum of row-parallel partials (:83-90) is an NCCL
   all-reduce over NVLink.  Embedding and lm_head are replicated (the reference
   does not shard them, model.py:50,115);
-* dense projections, RMSNorm (``norm.py:31-33``) and SwiGLU
-  (``kernels/triton/swiglu.py:103-107``) in PyTorch (cuBLAS) — harness, not the
-  optimisation target.
+* residual add + RMSNorm (``norm.py:31-33``), SwiGLU (``kernels/triton/swiglu.py:103-107``)
+  and the greedy argmax as CUDA kernels of this package; at TP > 1 the all-reduce of
+  the row-parallel partials can be the fused one-shot NVLink kernel that also does the
+  add + RMSNorm; dense projections on cuBLAS or the tcgen05 decode GEMM.
 
 ``decode_step`` allocates nothing and reads lengths on the device, so the whole
 step (all layers, all-reduces, lm_head, greedy argmax) is captured once in a
@@ -121,6 +124,20 @@ class Llama3DecodeModel:
         self.attn_core = None
         # Decode projections that run on the tcgen05 decode GEMM (the rest: F.linear).
         self.tc_projections = set(DEFAULT_TC_PROJECTIONS)
+        # Optional ``mark(phase)`` called after each phase of ``decode_step`` (profiling:
+        # e.g. records a timing event; phases are named in ``decode_step``).
+        self.mark = None
+
+    def _mark(self, phase: str) -> None:
+        if self.mark is not None:
+            self.mark(phase)
+
+    def check_status(self, cache: PagedKVCache) -> None:
+        """Synchronise and raise if a kernel of the step (attention, or the fused
+        all-reduce at TP > 1) reported an error through its status word."""
+        cache.check_status()
+        if self.tp.fused is not None:
+            self.tp.fused.check_status()
 
     # -- weights ---------------------------------------------------------------
     def _add_layer(self, full: dict) -> None:
@@ -219,14 +236,19 @@ class Llama3DecodeModel:
         v = v.view(B, S, self.hkv, d).transpose(1, 2)
         return q, k, v
 
-    def _mlp(self, L: dict, x: torch.Tensor) -> torch.Tensor:
+    def _mlp(self, L: dict, x: torch.Tensor, mark=None) -> torch.Tensor:
+        mark = mark or (lambda _: None)
         gu = self._linear(x, L["wgu"], "gate_up")
+        mark("gemm_gate_up")
         if gu.is_cuda:
             h = swiglu(gu)                                 # fused CUDA kernel
         else:
             gate, up = gu.split(self.inter, dim=-1)
             h = (gate * torch.sigmoid(gate)) * up         # swiglu.py:103-107
-        return self._linear(h, L["wdown"], "down")   # row-parallel partial
+        mark("swiglu")
+        out = self._linear(h, L["wdown"], "down")    # row-parallel partial
+        mark("gemm_down")
+        return out
 
     def _linear(self, x: torch.Tensor, w: torch.Tensor, name: str) -> torch.Tensor:
         """``x @ w.T`` for the projection ``name``: the tcgen05 decode GEMM when ``name``
@@ -308,23 +330,34 @@ class Llama3DecodeModel:
         """One token per sequence: ``ids [B]`` -> logits ``[B, vocab]``."""
         cfg = self.cfg
         B = ids.shape[0]
+        mark = self._mark
         x = F.embedding(ids.view(B, 1), self.embed)          # [B, 1, H]
+        mark("embed")
         delta = None
         for li, L in enumerate(self.layers):
             lc = cache.get_layer(li)
             x, h = self._reduce_add_norm(x, L["in_norm"], delta)
+            mark("allreduce_add_norm" if delta is not None else "add_norm")
             q, k, v = self._split_qkv(self._linear(h, L["wqkv"], "qkv"), B, 1)
+            mark("gemm_qkv")
             if self.attn_core is not None:
                 attn = self.attn_core(li, q, k, v, lc)
             else:
                 # RoPE + page append + paged attention in one fused decode launch
                 attn = lc.rope_append_decode(q, k, v, self.rope,
                                              partition_tokens=partition_tokens)
+            mark("attention")
             attn = attn.reshape(B, 1, self.hq * cfg.head_dim)
-            x, h = self._reduce_add_norm(x, L["post_norm"], self._linear(attn, L["wo"], "o"))
-            delta = self._mlp(L, h)
+            partial = self._linear(attn, L["wo"], "o")
+            mark("gemm_o")
+            x, h = self._reduce_add_norm(x, L["post_norm"], partial)
+            mark("allreduce_add_norm")
+            delta = self._mlp(L, h, mark)
         x, h = self._reduce_add_norm(x, self.final_norm, delta)
-        return self._lm_head(h[:, 0])
+        mark("allreduce_add_norm")
+        logits = self._lm_head(h[:, 0])
+        mark("lm_head")
+        return logits
 
     def bytes_per_step(self, cache: PagedKVCache) -> tuple[int, int]:
         """(weight bytes, KV bytes) this rank reads in one decode step at the current
@@ -362,9 +395,11 @@ class DecodeGraph:
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
             with torch.cuda.graph(self.graph, stream=s):
+                model._mark("start")
                 self.logits = model.decode_step(self.ids, cache, partition_tokens)
                 argmax_rows(self.logits, out=self.next_ids)
                 self.ids.copy_(self.next_ids)
+                model._mark("argmax")
         torch.cuda.current_stream(model.device).wait_stream(s)
         torch.cuda.synchronize()
         self._reset(lens0, host0)

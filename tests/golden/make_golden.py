@@ -191,8 +191,11 @@ def gen_tiny_model(ref):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref-src", default=os.environ.get("LLMCUDA_REF_SRC", "/root/reference/src"))
+    ap.add_argument("--ref-src", default=os.environ.get("LLMCUDA_REF_SRC"),
+                    help="the reference's src/ directory (or set LLMCUDA_REF_SRC)")
     args = ap.parse_args()
+    if not args.ref_src:
+        ap.error("pass --ref-src <llm-cuda>/src or set LLMCUDA_REF_SRC")
     sys.path.insert(0, args.ref_src)
     from llm_cuda.models.llama3 import attention as ra
     from llm_cuda.models.llama3 import kv_cache as rk

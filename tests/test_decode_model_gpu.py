@@ -27,12 +27,12 @@ def test_tiny_llama_paged_decode_matches_reference():
     prefill = int(g["prefill"])
     cache = m.make_cache(1, 32, page_size=4, shuffle_seed=3)
     last = m.prefill(ids[:, :prefill], cache)
-    np.testing.assert_allclose(last.cpu().numpy(), g["full_logits"][:, prefill - 1], rtol=1e-4,
-                               atol=1e-4)
+    np.testing.assert_allclose(last.cpu().numpy(), g["full_logits"][:, prefill - 1], rtol=1e-5,
+                               atol=1e-5)
     steps = [m.decode_step(ids[:, i], cache) for i in range(prefill, ids.shape[1])]
     cache.check_status()
     got = torch.stack(steps, dim=1).cpu().numpy()
-    np.testing.assert_allclose(got, g["step_logits"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(got, g["step_logits"], rtol=1e-5, atol=1e-5)
 
 
 def _reference_attn_core(model):
@@ -102,11 +102,10 @@ def test_llama8b_shape_step_matches_reference_attention():
     b = m.decode_step(nxt, cache).float()
     m.attn_core = None
     cache.check_status()
-    # The 2e-2 bf16 bar is stated for N(0,1) inputs; model activations reach |out| ~ 4,
-    # where one bf16 ulp is already 0.03, so the bar is scaled by the output magnitude.
     o_ref = seen[("ref", 0)].float()
     att = (seen[("ours", 0)].float() - o_ref).abs().max().item()
-    assert att <= 2e-2 * max(1.0, o_ref.abs().max().item()), att
+    print(f"\nlayer-0 attention max|ours - ref| = {att:.3e} (max|ref| {o_ref.abs().max().item():.2f})")
+    assert att <= 2e-2, att
     scale = b.abs().max().item()
     assert (a - b).abs().max().item() <= 0.05 * scale
     assert (a.argmax(-1) == b.argmax(-1)).float().mean().item() >= 0.75
