@@ -303,22 +303,24 @@ LLMC_API int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype
  * process.
  *
  * Setup (once per TP group):
- *  - Every rank allocates two shared regions with llmc_ipc_alloc: recv of
- *    llmc_ar_region_bytes bytes, and flags of *flag_bytes bytes (both zero-filled).
+ *  - Every rank allocates one shared region with llmc_ipc_alloc, of
+ *    llmc_ar_region_bytes bytes (zero-filled).  *flag_bytes is set to 0: the protocol
+ *    needs no flag region.
  *  - The ranks exchange the llmc_ipc_handle_bytes()-byte handles, e.g. with
  *    torch.distributed.all_gather_object, and open the peers' with llmc_ipc_open.
- *  - Each rank builds two device arrays [world], recv_ptrs and flag_ptrs: rank q's
- *    pointers, its own included.
+ *  - Each rank builds a device array recv_ptrs [world]: rank q's region pointer, its
+ *    own included.  flag_ptrs is not used and may be NULL.
  *  - epoch is a zeroed int32 [rows_cap] on the rank's own GPU.
  *
  * Per call, on every rank with the same rows:
  *   sum = sum over ranks of partial (fp32 in rank order, rounded to the dtype);
  *   x += sum (rounded to the dtype); out = x * rsqrt(mean(x^2) + eps) * weight.
- * One launch, one CTA per row. A row pushes its partial to every rank, publishes its
- * epoch with a system-scope release, and waits, bounded at 2 s, for every rank's
- * row. On timeout LLMC_STATUS_WAIT_TIMEOUT is set, the row is left unchanged and the
- * row's epoch still advances. The ranks' epochs may then be out of step, so stop using
- * the regions and rebuild them. Calls must be issued in the same order on all ranks.
+ * One launch, one CTA per row. A row pushes its partial to every peer as 8-byte words
+ * that carry 4 bytes of data and the call's epoch, and polls, bounded at 2 s, until
+ * every peer's words of this epoch have arrived (no fence, no separate flag). On
+ * timeout LLMC_STATUS_WAIT_TIMEOUT is set, the row is left unchanged and the row's
+ * epoch still advances. The ranks' epochs may then be out of step, so stop using the
+ * regions and rebuild them. Calls must be issued in the same order on all ranks.
  */
 LLMC_API size_t llmc_ipc_handle_bytes(void);
 LLMC_API int llmc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);

@@ -9,15 +9,19 @@
 //
 // Transport (no NCCL, no multicast): every rank owns, in memory mapped by all peers
 // through CUDA IPC,
-//   recv  [2][world][rows_cap][hidden]  partial rows pushed by each rank (double buffer)
-//   flags [2][world][rows_cap] int32    epoch at which rank q's row b landed
+//   recv [2][world][rows_cap][hidden * elem / 4]  8-byte words {4 data bytes, epoch}
 // and keeps a private epoch counter per row.  CTA b of a call with epoch e:
-//   1. pushes its partial row b into recv[e & 1][rank][b] of every rank (P2P stores),
-//   2. fences at system scope and stores e into flags[e & 1][rank][b] of every rank,
-//   3. waits (bounded by %globaltimer) until flags[e & 1][q][b] == e for every q,
-//   4. sums the rows from its own recv (L2 reads), adds x and normalises.
-// A rank reaches epoch e + 2 (which reuses slot e & 1) only after every peer has
-// signalled e + 1, i.e. after every peer has finished reading slot e & 1 of call e.
+//   1. pushes its partial row b into recv[e & 1][rank][b] of every peer with 8-byte
+//      stores, each carrying 4 bytes of the row and the epoch e,
+//   2. polls (bounded by %globaltimer) its own recv[e & 1][q][b] of every peer q until
+//      every word carries e: an aligned 8-byte store is seen whole or not at all, so a
+//      word with epoch e holds this call's data, and no fence or separate flag (with
+//      its extra NVLink round trip) is needed,
+//   3. sums the rows in rank order (its own from registers), adds x and normalises.
+// Words from older calls carry older epochs, so nothing is ever cleared.  A rank
+// reaches epoch e + 2 (which reuses slot e & 1) only after every peer has sent its
+// e + 1 words, i.e. after every peer has finished call e (each call waits for the
+// previous kernel before it pushes).
 #include <string>
 
 #include "common.cuh"
@@ -25,12 +29,10 @@
 namespace llmc {
 namespace ar {
 
-constexpr int kMaxWorld = 8;
-
 struct Params {
   const void* partial;            // local [rows, hidden] (this rank's row-parallel output)
   void* const* recv;              // [world] device pointers to each rank's recv base
-  int32_t* const* flags;          // [world] device pointers to each rank's flags base
+  int32_t* const* flags;          // unused (the words carry their epoch)
   int32_t* epoch;                 // local [rows_cap]
   void* x;                        // [rows, hidden] residual, updated in place
   const void* w;                  // [hidden]
@@ -40,16 +42,16 @@ struct Params {
   float eps;
 };
 
-__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_ll(uint64_t* p, uint32_t data, uint32_t flag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(data), "r"(flag)
+               : "memory");
 }
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ void ld_ll(const uint64_t* p, uint32_t& data, uint32_t& flag) {
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(data), "=r"(flag) : "l"(p)
+               : "memory");
 }
 
-// One CTA per row; each thread owns NV 16-byte vectors of the row.
+// One CTA per row; each thread owns NV 16-byte vectors of the row (4 words each).
 template <typename T, int NV>
 __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Params p) {
   constexpr int VEC = 16 / sizeof(T);
@@ -66,63 +68,43 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
     s_fail = 0;
   }
   __syncthreads();
-  const int32_t e = s_epoch;
+  const uint32_t e = (uint32_t)s_epoch;
   const int par = e & 1;
-  const size_t row_elems = (size_t)p.hidden;
-  const size_t slot_stride = (size_t)p.world * p.rows_cap * row_elems;   // elements per parity
+  const size_t row_words = (size_t)nvec * 4;                       // 8-byte words per row
+  const size_t slot_words = (size_t)p.world * p.rows_cap * row_words;
 
-  // 1. push this rank's row b to every rank (itself included)
+  // 1. push this rank's row b to every peer (its own copy stays in registers)
   const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.partial) +
-                                                    (size_t)b * row_elems);
+                                                    (size_t)b * p.hidden);
   uint4 mine[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
     if (i < nvec) mine[k] = __ldcg(src + i);
   }
-  const size_t dst_off = (size_t)par * slot_stride +
-                         ((size_t)p.rank * p.rows_cap + b) * row_elems;
+  const size_t my_row = (size_t)par * slot_words + ((size_t)p.rank * p.rows_cap + b) * row_words;
   for (int q = 0; q < p.world; ++q) {
-    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.recv[q]) + dst_off);
+    if (q == p.rank) continue;
+    uint64_t* dst = reinterpret_cast<uint64_t*>(p.recv[q]) + my_row;
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const int i = threadIdx.x + k * blockDim.x;
-      if (i < nvec) dst[i] = mine[k];
-    }
-  }
-  // 2. make the pushes visible system-wide, then publish the epoch on every rank
-  __threadfence_system();
-  __syncthreads();
-  const size_t flag_off = (size_t)par * p.world * p.rows_cap + (size_t)p.rank * p.rows_cap + b;
-  if (threadIdx.x < p.world) st_release_sys(p.flags[threadIdx.x] + flag_off, e);
-  // 3. wait (bounded) for every rank's row b of this epoch
-  if (threadIdx.x < p.world) {
-    const int32_t* f = p.flags[p.rank] + (size_t)par * p.world * p.rows_cap +
-                       (size_t)threadIdx.x * p.rows_cap + b;
-    const unsigned long long t0 = globaltimer_ns();
-    unsigned it = 0;
-    while (ld_acquire_sys(f) != e) {
-      if ((++it & 255u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
-        atomicOr(p.status, kStatusWaitTimeout);
-        s_fail = 1;
-        break;
+      if (i < nvec) {   // word j of vector i at j * nvec + i: each store is warp-contiguous
+        st_ll(dst + 0 * nvec + i, mine[k].x, e);
+        st_ll(dst + 1 * nvec + i, mine[k].y, e);
+        st_ll(dst + 2 * nvec + i, mine[k].z, e);
+        st_ll(dst + 3 * nvec + i, mine[k].w, e);
       }
     }
   }
-  __syncthreads();
-  if (s_fail) {
-    // Rows stay as they were and the status word reports the timeout.  The epoch still
-    // advances: this rank has already published e to its peers, so reusing e on the
-    // next call would pass the wait on the peers' stale flags of this call.
-    if (threadIdx.x == 0) p.epoch[b] = e;
-    return;
-  }
-  // 4. sum in rank order from this rank's recv slot, add the residual, normalise
-  const T* rv = reinterpret_cast<const T*>(p.recv[p.rank]) + (size_t)par * slot_stride +
-                (size_t)b * row_elems;
-  T* xr = reinterpret_cast<T*>(p.x) + (size_t)b * row_elems;
+  // 2 + 3. sum in rank order: own row from registers, each peer's words polled until
+  // they carry this epoch (bounded wait), then the residual add and the norm
+  const uint64_t* rv = reinterpret_cast<const uint64_t*>(p.recv[p.rank]) + (size_t)par * slot_words;
+  T* xr = reinterpret_cast<T*>(p.x) + (size_t)b * p.hidden;
   float xs[NV][VEC];
   float ss = 0.f;
+  bool fail = false;
+  const unsigned long long t0 = globaltimer_ns();
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
@@ -131,7 +113,26 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
 #pragma unroll
     for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
     for (int q = 0; q < p.world; ++q) {
-      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(rv + (size_t)q * p.rows_cap * row_elems) + i);
+      uint4 v;
+      if (q == p.rank) {
+        v = mine[k];
+      } else {
+        const uint64_t* w = rv + ((size_t)q * p.rows_cap + b) * row_words + i;
+        uint32_t d[4], f[4];
+        unsigned it = 0;
+        for (;;) {
+          ld_ll(w + 0 * nvec, d[0], f[0]);
+          ld_ll(w + 1 * nvec, d[1], f[1]);
+          ld_ll(w + 2 * nvec, d[2], f[2]);
+          ld_ll(w + 3 * nvec, d[3], f[3]);
+          if (f[0] == e && f[1] == e && f[2] == e && f[3] == e) break;
+          if (fail || ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs)) {
+            fail = true;
+            break;
+          }
+        }
+        v = make_uint4(d[0], d[1], d[2], d[3]);
+      }
       const T* ve = reinterpret_cast<const T*>(&v);
 #pragma unroll
       for (int j = 0; j < VEC; ++j) acc[j] += to_f32(ve[j]);
@@ -145,6 +146,27 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
       xs[k][j] = to_f32(xe[j]);
       ss = fmaf(xs[k][j], xs[k][j], ss);
     }
+  }
+  if (fail) {
+    atomicOr(p.status, kStatusWaitTimeout);
+    s_fail = 1;
+  }
+  __syncthreads();
+  if (s_fail) {
+    // Rows stay as they were and the status word reports the timeout.  The epoch still
+    // advances: this rank has already pushed e-words to its peers, so reusing e on the
+    // next call could let a peer take this call's words for the next call's.
+    if (threadIdx.x == 0) p.epoch[b] = (int32_t)e;
+    return;
+  }
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nvec) continue;
+    uint4 xv;
+    T* xe = reinterpret_cast<T*>(&xv);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) xe[j] = from_f32<T>(xs[k][j]);
     reinterpret_cast<uint4*>(xr)[i] = xv;
   }
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -158,7 +180,7 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
   __syncthreads();
   const float r = rsqrtf(red[0] / p.hidden + p.eps);
   const uint4* wv = reinterpret_cast<const uint4*>(p.w);
-  uint4* hr = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h) + (size_t)b * row_elems);
+  uint4* hr = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h) + (size_t)b * p.hidden);
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
@@ -171,16 +193,17 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
     for (int j = 0; j < VEC; ++j) oe[j] = from_f32<T>(xs[k][j] * r * to_f32(we[j]));
     hr[i] = ov;
   }
-  if (threadIdx.x == 0) p.epoch[b] = e;
+  if (threadIdx.x == 0) p.epoch[b] = (int32_t)e;
 }
 
 }  // namespace ar
 
-// Sizes of one rank's shared region: recv (elements of the dtype), flags (int32).
+// Size of one rank's shared region: two parities of [world][rows_cap] rows of 8-byte
+// words, each carrying 4 bytes of the row.  No flag region is needed.
 size_t ar_recv_bytes(int world, int rows_cap, int hidden, int elem) {
-  return (size_t)2 * world * rows_cap * hidden * elem;
+  return (size_t)2 * world * rows_cap * ((size_t)hidden * elem / 4) * 8;
 }
-size_t ar_flag_bytes(int world, int rows_cap) { return (size_t)2 * world * rows_cap * 4; }
+size_t ar_flag_bytes(int, int) { return 0; }
 
 cudaError_t launch_allreduce_add_rmsnorm(const ar::Params& p, int dtype, std::string* err,
                                          cudaStream_t stream) {

@@ -438,7 +438,7 @@ int llmc_allreduce_add_rmsnorm(const void* partial, void* const* recv_ptrs,
     return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: need 0 <= rank < world <= 8");
   if (rows < 0 || rows > rows_cap || hidden <= 0)
     return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: need 0 <= rows <= rows_cap, hidden > 0");
-  if (!partial || !recv_ptrs || !flag_ptrs || !epoch || !x || !weight || !out || !status)
+  if (!partial || !recv_ptrs || !epoch || !x || !weight || !out || !status)
     return fail(LLMC_EINVAL, "llmc_allreduce_add_rmsnorm: NULL pointer argument");
   auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (!al(partial) || !al(x) || !al(weight) || !al(out))

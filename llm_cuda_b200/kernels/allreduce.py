@@ -4,10 +4,11 @@ Replaces, for the decode rows of a tensor-parallel step, the NCCL all-reduce of 
 row-parallel o_proj / down_proj partials (the in-process sum of
 ``src/llm_cuda/parallel/tensor_parallel.py:83-90`` of llm-cuda) and the residual add +
 RMSNorm that follows it (``models/llama3/model.py:37-42``, ``norm.py:31-33``) with one
-kernel per call (``llmc_allreduce_add_rmsnorm``).  The ranks' receive buffers and
-flags are plain device allocations shared through CUDA IPC handles, exchanged once
-over the process group; the kernel moves data with peer stores over NVLink and
-synchronises with per-row epoch flags (bounded waits, no multicast).
+kernel per call (``llmc_allreduce_add_rmsnorm``).  Each rank's receive
+region is a plain device allocation shared through a CUDA IPC handle, exchanged once
+over the process group; the kernel pushes each row to the peers as 8-byte words that
+carry their own epoch, so a receiver knows a word has arrived without any fence or
+separate flag (bounded waits, no multicast).
 """
 
 from __future__ import annotations
@@ -40,35 +41,29 @@ class NvlinkAllReduce:
         fb = ctypes.c_size_t(0)
         with torch.cuda.device(self.device):
             rb = self.lib.llmc_ar_region_bytes(world, rows_cap, hidden, dt, ctypes.byref(fb))
+            if fb.value:
+                raise RuntimeError("llmc_ar_region_bytes asks for a flag region this binding "
+                                   "does not allocate")
             hsz = self.lib.llmc_ipc_handle_bytes()
-            self._own = []
-            handles = []
-            for nbytes in (rb, fb.value):
-                ptr = ctypes.c_void_p()
-                h = ctypes.create_string_buffer(hsz)
-                N.check(self.lib.llmc_ipc_alloc(nbytes, ctypes.byref(ptr), h), "llmc_ipc_alloc")
-                self._own.append(ptr.value)
-                handles.append(h.raw)
+            ptr = ctypes.c_void_p()
+            h = ctypes.create_string_buffer(hsz)
+            N.check(self.lib.llmc_ipc_alloc(rb, ctypes.byref(ptr), h), "llmc_ipc_alloc")
+            self._own = [ptr.value]
             gathered = [None] * world
-            dist.all_gather_object(gathered, handles, group=group)
+            dist.all_gather_object(gathered, h.raw, group=group)
             self._opened = []
-            recv, flags = [], []
+            recv = []
             for q in range(world):
                 if q == rank:
                     recv.append(self._own[0])
-                    flags.append(self._own[1])
                     continue
-                ptrs = []
-                for h in gathered[q]:
-                    ptr = ctypes.c_void_p()
-                    N.check(self.lib.llmc_ipc_open(ctypes.create_string_buffer(h, len(h)),
-                                                   ctypes.byref(ptr)), "llmc_ipc_open")
-                    self._opened.append(ptr.value)
-                    ptrs.append(ptr.value)
-                recv.append(ptrs[0])
-                flags.append(ptrs[1])
+                hq = gathered[q]
+                ptr = ctypes.c_void_p()
+                N.check(self.lib.llmc_ipc_open(ctypes.create_string_buffer(hq, len(hq)),
+                                               ctypes.byref(ptr)), "llmc_ipc_open")
+                self._opened.append(ptr.value)
+                recv.append(ptr.value)
         self.recv_ptrs = torch.tensor(recv, dtype=torch.int64, device=self.device)
-        self.flag_ptrs = torch.tensor(flags, dtype=torch.int64, device=self.device)
         self.epoch = torch.zeros(rows_cap, dtype=torch.int32, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.failed = False     # set once a wait timeout has been reported
@@ -92,7 +87,7 @@ class NvlinkAllReduce:
         w = weight if weight.dtype == x.dtype else weight.to(x.dtype)
         out = torch.empty_like(x) if out is None else out
         rc = self.lib.llmc_allreduce_add_rmsnorm(
-            partial.data_ptr(), self.recv_ptrs.data_ptr(), self.flag_ptrs.data_ptr(),
+            partial.data_ptr(), self.recv_ptrs.data_ptr(), None,
             self.epoch.data_ptr(), x.data_ptr(), w.contiguous().data_ptr(), out.data_ptr(),
             self.status.data_ptr(), self.rank, self.world, rows, self.rows_cap, self.hidden,
             float(eps), N.dtype_code(x.dtype), N.stream_handle(x.device))
