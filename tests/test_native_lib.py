@@ -114,8 +114,10 @@ def test_host_validation_of_step_entry_points():
                                         1e-5, N.LLMC_BF16, nul)
     assert rc == -1 and b"aligned" in lib.llmc_last_error_string()
     fb = ctypes.c_size_t(0)
-    assert lib.llmc_ar_region_bytes(2, 64, 4096, N.LLMC_BF16, ctypes.byref(fb)) == 2 * 2 * 64 * 4096 * 2
-    assert fb.value == 2 * 2 * 64 * 4
+    # two parities x 2 ranks x 64 rows of 8-byte words, each carrying 4 bytes of a row
+    assert lib.llmc_ar_region_bytes(2, 64, 4096, N.LLMC_BF16, ctypes.byref(fb)) == \
+        2 * 2 * 64 * (4096 * 2 // 4) * 8
+    assert fb.value == 0
     # argmax
     assert lib.llmc_argmax(1, 1, 70000, 10, N.LLMC_BF16, 8, nul) == -1
     assert lib.llmc_argmax(1, 1, 4, 10, N.LLMC_BF16, 4, nul) == -1        # misaligned workspace
