@@ -49,8 +49,19 @@ typedef struct CUstream_st* llmc_stream_t; /* == cudaStream_t */
 #define LLMC_STATUS_ROPE_RANGE 8
 #define LLMC_STATUS_SEQLEN_RANGE 16
 
-/* llmc_paged_decode flags */
+/* llmc_paged_decode / llmc_rope_append_decode_strided flags */
 #define LLMC_DECODE_FORCE_GENERIC 1 /* use the SIMT kernel even where the TMA kernel applies */
+/*
+ * LLMC_DECODE_EARLY_TABLES (balanced split only; ignored otherwise): the caller
+ * guarantees that seq_lens, block_table and the page pools are not written by any
+ * kernel that can still be running when this launch begins under programmatic
+ * dependent launch (the kernel just before it on the stream, or one before that which
+ * it has let start early).  The kernel then scans the lengths, splits the work and
+ * starts streaming K/V before it waits for the previous kernel; only the query, the
+ * new token's k/v and every write wait.  A decode step whose tables are touched only
+ * by this layer's own launch (and by the host between steps) qualifies.
+ */
+#define LLMC_DECODE_EARLY_TABLES 2
 
 /*
  * Fused RoPE-on-new-tokens + KV-page append.
@@ -146,7 +157,7 @@ LLMC_API int llmc_decode_balanced_supported(const void* q, const void* k_pages,
  *   part_o/part_lse: see llmc_decode_partials_bytes with
  *     max_parts = llmc_num_partitions(max_pages_per_seq * page_size, partition_tokens);
  *     may be NULL when max_parts == 1.
- *   flags: LLMC_DECODE_FORCE_GENERIC or 0.
+ *   flags: LLMC_DECODE_FORCE_GENERIC, LLMC_DECODE_EARLY_TABLES (ORed), or 0.
  * The hot kernel (bf16/fp16, d in {64,128,256}) is a persistent TMA + mbarrier
  * pipeline with tensor-core (mma.sync) tiles, one CTA per SM; other shapes use a
  * SIMT kernel with the same partial format.
@@ -197,7 +208,7 @@ LLMC_API int llmc_rope_append_decode(const void* q, const void* k_new, const voi
  * which saves three copies per layer.
  * Dense strides (Hq*d, Hkv*d) behave exactly as llmc_rope_append_decode. Other
  * strides need the fused kernel's shapes (bf16/fp16, d in {64, 128, 256}) and get
- * LLMC_EUNSUPPORTED otherwise.
+ * LLMC_EUNSUPPORTED otherwise.  flags: LLMC_DECODE_EARLY_TABLES or 0.
  */
 LLMC_API int llmc_rope_append_decode_strided(
     const void* q, const void* k_new, const void* v_new, void* q_rot_out, void* k_pages,
@@ -205,7 +216,7 @@ LLMC_API int llmc_rope_append_decode_strided(
     const void* sin_tab, int rope_max_pos, void* out, float* part_o, float* part_lse,
     int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d, int page_size,
     int max_pages_per_seq, int num_pages, int partition_tokens, float scale, int dtype,
-    long long q_seq_stride, long long kv_seq_stride, llmc_stream_t stream);
+    long long q_seq_stride, long long kv_seq_stride, int flags, llmc_stream_t stream);
 
 /*
  * Log-sum-exp merge of split-K partials into out [B, Hq, d].  For each (b, h)

@@ -17,6 +17,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "li
 
 LLMC_F32, LLMC_F16, LLMC_BF16 = 0, 1, 2
 LLMC_DECODE_FORCE_GENERIC = 1
+LLMC_DECODE_EARLY_TABLES = 2
 
 STATUS_BITS = {
     1: "pipeline wait timeout",
@@ -42,7 +43,8 @@ SIGNATURES = {
     "llmc_paged_decode_noalloc_capacity_bytes": (_SZ, []),
     "llmc_rope_append_decode": (_I, [_P] * 10 + [_I] + [_P] * 5 + [_I] * 8 + [_F, _I, _P]),
     "llmc_rope_append_decode_strided": (_I, [_P] * 10 + [_I] + [_P] * 5 + [_I] * 8
-                                        + [_F, _I, ctypes.c_longlong, ctypes.c_longlong, _P]),
+                                        + [_F, _I, ctypes.c_longlong, ctypes.c_longlong, _I,
+                                           _P]),
     "llmc_decode_gemm_workspace_bytes": (_SZ, [_I, _I, _I]),
     "llmc_decode_gemm": (_I, [_P, _P, _P, _P, _SZ, _P, _I, _I, _I, _P, _P]),
     "llmc_add_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _I, _P]),

@@ -22,6 +22,8 @@
 // reaches epoch e + 2 (which reuses slot e & 1) only after every peer has sent its
 // e + 1 words, i.e. after every peer has finished call e (each call waits for the
 // previous kernel before it pushes).
+#include <cstdlib>
+#include <cstring>
 #include <string>
 
 #include "common.cuh"
@@ -196,12 +198,225 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
   if (threadIdx.x == 0) p.epoch[b] = (int32_t)e;
 }
 
+// Two-shot variant for larger groups: the one-shot push costs (world - 1) full rows per
+// rank, this one 2 * (world - 1) / world of a row, at the price of a second hop.
+//   1. reduce-scatter: rank r owns the vectors [r * nvs, (r + 1) * nvs) of every row
+//      (nvs = vectors / world); every rank pushes each vector to its owner;
+//   2. the owner sums its slice in rank order, adds the residual (x_new), and reduces
+//      the slice's sum of squares;
+//   3. all-gather: the owner pushes x_new of its slice and that sum to every rank;
+//   4. every rank sums the slice sums in rank order (the same bits on every rank) and
+//      normalises the full row.
+// Region: RS area [2][world][rows_cap][4 * nvs] words, then AG area
+// [2][world][rows_cap][4 * nvs + 1] words (the last word of an AG row is the slice's
+// sum of squares).
+template <typename T, int NV>
+__global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_2shot_kernel(const Params p) {
+  constexpr int VEC = 16 / sizeof(T);
+  const int b = blockIdx.x;
+  const int nvec = p.hidden / VEC;
+  const int nvs = nvec / p.world;                 // vectors per owner slice
+  const size_t sw = (size_t)4 * nvs;              // words per slice
+  __shared__ int32_t s_epoch;
+  __shared__ int s_fail;
+  __shared__ float red[32];
+  __shared__ float s_part[8];
+  pdl_launch_dependents();
+  pdl_wait();   // the partial and x come from the previous kernels
+
+  if (threadIdx.x == 0) {
+    s_epoch = p.epoch[b] + 1;
+    s_fail = 0;
+  }
+  __syncthreads();
+  const uint32_t e = (uint32_t)s_epoch;
+  const int par = e & 1;
+  const size_t rs_par = (size_t)p.world * p.rows_cap * sw;           // RS words per parity
+  const size_t ag_base = 2 * rs_par;
+  const size_t ag_par = (size_t)p.world * p.rows_cap * (sw + 1);
+  uint64_t* own = reinterpret_cast<uint64_t*>(p.recv[p.rank]);
+
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(p.partial) +
+                                                    (size_t)b * p.hidden);
+  T* xr = reinterpret_cast<T*>(p.x) + (size_t)b * p.hidden;
+  uint4 mine[NV];
+  bool fail = false;
+  const unsigned long long t0 = globaltimer_ns();
+  auto poll4 = [&](const uint64_t* w, size_t stride, uint4& v) {
+    uint32_t d[4], f[4];
+    unsigned it = 0;
+    for (;;) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ld_ll(w + j * stride, d[j], f[j]);
+      if (f[0] == e && f[1] == e && f[2] == e && f[3] == e) break;
+      if (fail || ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs)) {
+        fail = true;
+        break;
+      }
+    }
+    v = make_uint4(d[0], d[1], d[2], d[3]);
+  };
+  // 1. reduce-scatter push: vector i goes to its owner i / nvs
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nvec) continue;
+    mine[k] = __ldcg(src + i);
+    const int q = i / nvs, li = i - q * nvs;
+    if (q == p.rank) continue;
+    uint64_t* dst = reinterpret_cast<uint64_t*>(p.recv[q]) + (size_t)par * rs_par +
+                    ((size_t)p.rank * p.rows_cap + b) * sw + li;
+    st_ll(dst + 0 * nvs, mine[k].x, e);
+    st_ll(dst + 1 * nvs, mine[k].y, e);
+    st_ll(dst + 2 * nvs, mine[k].z, e);
+    st_ll(dst + 3 * nvs, mine[k].w, e);
+  }
+  // 2. the owned slice: sum in rank order, residual add, sum of squares
+  float xs[NV][VEC];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nvec || i / nvs != p.rank) continue;
+    const int li = i - p.rank * nvs;
+    float acc[VEC];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+    for (int q = 0; q < p.world; ++q) {
+      uint4 v;
+      if (q == p.rank) v = mine[k];
+      else poll4(own + (size_t)par * rs_par + ((size_t)q * p.rows_cap + b) * sw + li, nvs, v);
+      const T* ve = reinterpret_cast<const T*>(&v);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) acc[j] += to_f32(ve[j]);
+    }
+    const uint4 xv = reinterpret_cast<const uint4*>(xr)[i];
+    const T* xe = reinterpret_cast<const T*>(&xv);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      xs[k][j] = to_f32(from_f32<T>(to_f32(xe[j]) + to_f32(from_f32<T>(acc[j]))));
+      ss = fmaf(xs[k][j], xs[k][j], ss);
+    }
+  }
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) s_part[p.rank] = t;
+  }
+  __syncthreads();
+  // 3. all-gather push: x_new of the owned slice, then the slice's sum of squares
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nvec || i / nvs != p.rank) continue;
+    const int li = i - p.rank * nvs;
+    uint4 xv;
+    T* xe = reinterpret_cast<T*>(&xv);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) xe[j] = from_f32<T>(xs[k][j]);
+    mine[k] = xv;   // this rank's own x_new vector
+    for (int q = 0; q < p.world; ++q) {
+      if (q == p.rank) continue;
+      uint64_t* dst = reinterpret_cast<uint64_t*>(p.recv[q]) + ag_base + (size_t)par * ag_par +
+                      ((size_t)p.rank * p.rows_cap + b) * (sw + 1) + li;
+      st_ll(dst + 0 * nvs, xv.x, e);
+      st_ll(dst + 1 * nvs, xv.y, e);
+      st_ll(dst + 2 * nvs, xv.z, e);
+      st_ll(dst + 3 * nvs, xv.w, e);
+    }
+  }
+  if (threadIdx.x < p.world && threadIdx.x != p.rank) {
+    uint64_t* dst = reinterpret_cast<uint64_t*>(p.recv[threadIdx.x]) + ag_base +
+                    (size_t)par * ag_par + ((size_t)p.rank * p.rows_cap + b) * (sw + 1) + sw;
+    st_ll(dst, __float_as_uint(s_part[p.rank]), e);
+  }
+  // 4. the other slices and the slice sums
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nvec) continue;
+    const int q = i / nvs, li = i - q * nvs;
+    if (q == p.rank) continue;
+    uint4 v;
+    poll4(own + ag_base + (size_t)par * ag_par + ((size_t)q * p.rows_cap + b) * (sw + 1) + li,
+          nvs, v);
+    mine[k] = v;
+    const T* ve = reinterpret_cast<const T*>(&v);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) xs[k][j] = to_f32(ve[j]);
+  }
+  if (threadIdx.x < p.world && threadIdx.x != p.rank) {
+    const uint64_t* w = own + ag_base + (size_t)par * ag_par +
+                        ((size_t)threadIdx.x * p.rows_cap + b) * (sw + 1) + sw;
+    uint32_t d = 0, f = 0;
+    unsigned it = 0;
+    for (;;) {
+      ld_ll(w, d, f);
+      if (f == e) break;
+      if (fail || ((++it & 63u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs)) {
+        fail = true;
+        break;
+      }
+    }
+    s_part[threadIdx.x] = __uint_as_float(d);
+  }
+  if (fail) {
+    atomicOr(p.status, kStatusWaitTimeout);
+    s_fail = 1;
+  }
+  __syncthreads();
+  if (s_fail) {
+    if (threadIdx.x == 0) p.epoch[b] = (int32_t)e;   // as in the one-shot kernel
+    return;
+  }
+  float tot = 0.f;
+  for (int q = 0; q < p.world; ++q) tot += s_part[q];   // rank order: the same on every rank
+  const float r = rsqrtf(tot / p.hidden + p.eps);
+  const uint4* wv = reinterpret_cast<const uint4*>(p.w);
+  uint4* hr = reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h) + (size_t)b * p.hidden);
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= nvec) continue;
+    reinterpret_cast<uint4*>(xr)[i] = mine[k];
+    const uint4 ww = __ldg(wv + i);
+    const T* we = reinterpret_cast<const T*>(&ww);
+    uint4 ov;
+    T* oe = reinterpret_cast<T*>(&ov);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) oe[j] = from_f32<T>(xs[k][j] * r * to_f32(we[j]));
+    hr[i] = ov;
+  }
+  if (threadIdx.x == 0) p.epoch[b] = (int32_t)e;
+}
+
 }  // namespace ar
 
 // Size of one rank's shared region: two parities of [world][rows_cap] rows of 8-byte
 // words, each carrying 4 bytes of the row.  No flag region is needed.
+// The region holds either layout: one-shot 2 * world * rows_cap * W words (W = words
+// per row), two-shot 2 * rows_cap * W words of reduce-scatter slices plus
+// 2 * world * rows_cap * (W / world + 1) words of all-gather slices with their sums.
 size_t ar_recv_bytes(int world, int rows_cap, int hidden, int elem) {
-  return (size_t)2 * world * rows_cap * ((size_t)hidden * elem / 4) * 8;
+  const size_t w = (size_t)hidden * elem / 4;
+  const size_t one = (size_t)2 * world * rows_cap * w;
+  const size_t two = (size_t)2 * rows_cap * w + (size_t)2 * world * rows_cap * (w / world + 1);
+  return (one > two ? one : two) * 8;
+}
+
+// One-shot up to `kOneShotMaxWorld` ranks, two-shot above, unless LLMC_AR_ALGO names
+// one ("one_shot" / "two_shot"; read once per process, for measurements).
+constexpr int kOneShotMaxWorld = 2;
+static int ar_algo_override() {
+  static int v = -1;
+  if (v < 0) {
+    const char* s = getenv("LLMC_AR_ALGO");
+    v = (s && !strcmp(s, "one_shot")) ? 1 : (s && !strcmp(s, "two_shot")) ? 2 : 0;
+  }
+  return v;
 }
 size_t ar_flag_bytes(int, int) { return 0; }
 
@@ -227,7 +442,12 @@ cudaError_t launch_allreduce_add_rmsnorm(const ar::Params& p, int dtype, std::st
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-#define LLMC_AR(TT, NV) cudaLaunchKernelEx(&cfg, ar::allreduce_add_rmsnorm_kernel<TT, NV>, p)
+  const int ov = ar_algo_override();
+  const bool two = nvec % p.world == 0 && p.world > 1 &&
+                   (ov == 2 || (ov == 0 && p.world > kOneShotMaxWorld));
+#define LLMC_AR(TT, NV)                                                                      \
+  (two ? cudaLaunchKernelEx(&cfg, ar::allreduce_add_rmsnorm_2shot_kernel<TT, NV>, p)        \
+       : cudaLaunchKernelEx(&cfg, ar::allreduce_add_rmsnorm_kernel<TT, NV>, p))
 #define LLMC_AR_T(TT)                                          \
   do {                                                         \
     if (nv == 1) e = LLMC_AR(TT, 1);                           \

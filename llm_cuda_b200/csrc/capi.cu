@@ -30,7 +30,7 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
                                 int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
                                 int D, int P, int max_pages, int num_pages, int Tpart,
                                 float scale, int dtype, std::string* err, cudaStream_t stream,
-                                long long q_stride, long long kv_stride);
+                                long long q_stride, long long kv_stride, int flags);
 cudaError_t launch_decode_gemm(const void* x, const void* w, void* y, float* ws, size_t ws_floats,
                                int32_t* counters, int Mb, int N, int K, int32_t* status,
                                std::string* err, cudaStream_t stream);
@@ -214,7 +214,7 @@ int llmc_rope_append_decode_strided(
     const void* sin_tab, int rope_max_pos, void* out, float* part_o, float* part_lse,
     int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv, int d, int page_size,
     int max_pages_per_seq, int num_pages, int partition_tokens, float scale, int dtype,
-    long long q_seq_stride, long long kv_seq_stride, llmc_stream_t stream) {
+    long long q_seq_stride, long long kv_seq_stride, int flags, llmc_stream_t stream) {
   g_last_error.clear();
   const bool dense = q_seq_stride == (long long)Hq * d && kv_seq_stride == (long long)Hkv * d;
   if (q_seq_stride < (long long)Hq * d || kv_seq_stride < (long long)Hkv * d)
@@ -248,7 +248,7 @@ int llmc_rope_append_decode_strided(
       q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens, cos_tab, sin_tab,
       rope_max_pos, out, part_o, part_lse, lens_next, status, B, Hq, Hkv, d, page_size,
       max_pages_per_seq, num_pages, partition_tokens, scale, dtype, &err, (cudaStream_t)stream,
-      q_seq_stride, kv_seq_stride);
+      q_seq_stride, kv_seq_stride, flags);
   if (e == cudaErrorNotSupported && !dense)
     return fail(LLMC_EUNSUPPORTED,
                 "llmc_rope_append_decode: strided q/k/v need the fused kernel's shapes");
@@ -302,7 +302,7 @@ int llmc_rope_append_decode(const void* q, const void* k_new, const void* v_new,
       q, k_new, v_new, q_rot_out, k_pages, v_pages, block_table, seq_lens, cos_tab, sin_tab,
       rope_max_pos, out, part_o, part_lse, lens_next, status, B, Hq, Hkv, d, page_size,
       max_pages_per_seq, num_pages, partition_tokens, scale, dtype, (long long)Hq * d,
-      (long long)Hkv * d, stream);
+      (long long)Hkv * d, 0, stream);
 }
 
 size_t llmc_decode_gemm_workspace_bytes(int Mb, int N, int K) {

@@ -109,6 +109,11 @@ struct Params {
   long long q_stride;      // elements between the queries of consecutive sequences
   long long kv_stride;     // the same for k_new / v_new (heads are D apart in both)
   int32_t* seq_lens_out;   // FUSE + balanced: lengths after the step are written here
+  // Balanced split only: seq_lens, the block table and the page pools are not written
+  // by any kernel that can still be running when this one starts, so the length scan,
+  // the work split and the K/V stream begin before griddepcontrol.wait; only the
+  // roles that read the previous kernel's output (q, new k/v) or write anything wait.
+  int early;
 };
 
 // Byte offset of (row, 16-byte chunk) inside a 128B-swizzled region whose base is
@@ -458,8 +463,10 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
     }
   }
   // Everything above overlaps the previous kernel under programmatic dependent
-  // launch; lengths, block table and pages are read only after this wait.
-  pdl_wait();
+  // launch; lengths, block table and pages are read only after this wait, unless the
+  // caller vouched for them (p.early), in which case the consumer and merge warps wait
+  // below, before their first read of the previous kernel's output or first write.
+  if (!p.early) pdl_wait();
   pdl_launch_dependents();
   if (warp == kConsumers) {
     const int per = (p.B + 31) / 32;
@@ -505,6 +512,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   if (warp == kMergeWarp) {
     // ======================= merge warp =======================
     if (!p.balanced) return;
+    if (p.early) pdl_wait();
     const int n_rows = p.B * p.Hkv * p.HG;
     // Empty contexts have no chunk: their rows get acc / max(l, 1e-9) = 0 here.
     for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
@@ -659,6 +667,7 @@ paged_decode_tma_kernel(const __grid_constant__ CUtensorMap tmap_k,
   }
 
   // ======================= consumer warps =======================
+  if (p.early) pdl_wait();   // q, the new token's k/v, and every write come after it
   const int g = lane >> 2;   // fragment row group
   const int c = lane & 3;    // fragment column pair
   const T* qbase = reinterpret_cast<const T*>(p.q);
@@ -1447,7 +1456,7 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
                                 int32_t* lens_next, int32_t* status, int B, int Hq, int Hkv,
                                 int D, int P, int max_pages, int num_pages, int Tpart,
                                 float scale, int dtype, std::string* err, cudaStream_t stream,
-                                long long q_stride, long long kv_stride) {
+                                long long q_stride, long long kv_stride, int flags) {
   if (B == 0) return cudaSuccess;
   if (!fast_path_applies(dtype, D, P, max_pages, Tpart, B, q_raw, kp, vp))
     return cudaErrorNotSupported;
@@ -1466,6 +1475,7 @@ cudaError_t launch_fused_decode(const void* q_raw, const void* k_new, const void
   p.k_pages = kp; p.v_pages = vp; p.q_rot_out = q_rot_out; p.lens_next = lens_next;
   p.rope_max_pos = rope_max_pos;
   p.seq_lens_out = seq_lens;
+  p.early = (flags & LLMC_DECODE_EARLY_TABLES) && p.balanced ? 1 : 0;
   cudaError_t e = launch_fast<true>(p, dtype, D, kp, vp, err, stream);
   if (e != cudaSuccess) return e;
   if (p.balanced) return cudaSuccess;   // merged and published inside the decode kernel
@@ -1502,6 +1512,7 @@ cudaError_t launch_paged_decode(const void* q, const void* kp, const void* vp, c
     p.lens_next = nullptr;
     p.rope_max_pos = 0;
     p.seq_lens_out = nullptr;
+    p.early = (flags & LLMC_DECODE_EARLY_TABLES) && p.balanced ? 1 : 0;
     return launch_fast<false>(p, dtype, D, kp, vp, err, stream);
   }
   // generic SIMT path

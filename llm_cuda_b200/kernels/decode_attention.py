@@ -285,6 +285,7 @@ def rope_append_decode(
     workspace: DecodeWorkspace | None = None,
     status: torch.Tensor | None = None,
     events=None,
+    early_tables: bool = False,
 ) -> torch.Tensor:
     """One fused decode-attention step (``llmc_rope_append_decode``).
 
@@ -294,6 +295,9 @@ def rope_append_decode(
     also advances ``seq_lens``.  ``host_lens`` are the lengths BEFORE the step.
     Returns ``out`` shaped like ``q``; the rotated query goes to ``q_out``.
     ``events``: optional CUDA-event pair recorded around the step's launches.
+    ``early_tables``: promise that no kernel still running when this one starts writes
+    ``seq_lens``, ``block_table`` or the pages (``LLMC_DECODE_EARLY_TABLES``): the K/V
+    stream then starts before the wait for the previous kernel.
     """
     lib = N.load()
     if not q.is_cuda:
@@ -320,7 +324,7 @@ def rope_append_decode(
         return t.stride(0)
     qs, ks, vs = seq_stride(q, Hq), seq_stride(k, Hkv), seq_stride(v, Hkv)
     strided = (qs is not None and ks is not None and ks == vs and partition_tokens == BALANCED
-               and (qs, ks) != (Hq * d, Hkv * d)
+               and ((qs, ks) != (Hq * d, Hkv * d) or early_tables)
                and lib.llmc_decode_balanced_supported(q.data_ptr(), key_pages.data_ptr(),
                                                       value_pages.data_ptr(),
                                                       N.dtype_code(q.dtype), d, P, max_pages, B))
@@ -346,7 +350,8 @@ def rope_append_decode(
             ws.lens_next(B).data_ptr(), st.data_ptr(), B, Hq, Hkv, d, P, max_pages, num_pages,
             partition_tokens, float(scale), N.dtype_code(q.dtype))
     if strided:
-        rc = lib.llmc_rope_append_decode_strided(*args, qs, ks, N.stream_handle(q.device))
+        flags = N.LLMC_DECODE_EARLY_TABLES if early_tables else 0
+        rc = lib.llmc_rope_append_decode_strided(*args, qs, ks, flags, N.stream_handle(q.device))
     else:
         rc = lib.llmc_rope_append_decode(*args, N.stream_handle(q.device))
     if events is not None:   # brackets the decode and merge launches of the step

@@ -40,10 +40,14 @@ from .rotary import RopeTable
 
 
 # Layer projections of the decode step served by the tcgen05 decode GEMM by default.
-# Measured at B=64 inside the whole-step graph, cuBLAS is still ahead on the layer
-# shapes (qkv 11.0 vs 14.6 us, gate_up 41.6 vs 48.5 us), so none are by default; the
-# vocabulary projection (lm_head) always uses the tcgen05 GEMM, which is faster there.
+# Measured at B=64 in CUDA graphs of back-to-back calls with weights larger than L2,
+# cuBLAS is ahead on the full-size layer shapes (qkv 11.9 vs 14.9 us, gate_up 42.5 vs
+# 50.8 us), so none are by default at TP1-2; the vocabulary projection (lm_head) always
+# uses the tcgen05 GEMM (176 vs 184 us).  On one rank's q/k/v at TP >= 4 the tcgen05
+# GEMM is ahead (1536 x 4096: 6.8 vs 8.2 us; 768 x 4096: 5.4 vs 7.8 us), and it lets
+# the attention launch after it start early (programmatic dependent launch).
 DEFAULT_TC_PROJECTIONS = ()
+TC_PROJECTIONS_TP4_UP = ("qkv",)
 
 
 @dataclass
@@ -123,10 +127,13 @@ class Llama3DecodeModel:
         # taking the raw (un-rotated) q/k/v; tests of the TP plumbing on CPU ranks use it.
         self.attn_core = None
         # Decode projections that run on the tcgen05 decode GEMM (the rest: F.linear).
-        self.tc_projections = set(DEFAULT_TC_PROJECTIONS)
+        self.tc_projections = set(DEFAULT_TC_PROJECTIONS if N < 4 else TC_PROJECTIONS_TP4_UP)
         # Optional ``mark(phase)`` called after each phase of ``decode_step`` (profiling:
         # e.g. records a timing event; phases are named in ``decode_step``).
         self.mark = None
+        # Attention launches may start their K/V stream before the previous kernel ends
+        # (LLMC_DECODE_EARLY_TABLES): nothing else in the step writes a layer's tables.
+        self.early_tables = True
 
     def _mark(self, phase: str) -> None:
         if self.mark is not None:
@@ -343,9 +350,13 @@ class Llama3DecodeModel:
             if self.attn_core is not None:
                 attn = self.attn_core(li, q, k, v, lc)
             else:
-                # RoPE + page append + paged attention in one fused decode launch
+                # RoPE + page append + paged attention in one fused decode launch.  A
+                # layer's lengths, block table and pages are written only by its own
+                # attention launch (and the host between steps), so the K/V stream may
+                # start before the QKV projection has finished.
                 attn = lc.rope_append_decode(q, k, v, self.rope,
-                                             partition_tokens=partition_tokens)
+                                             partition_tokens=partition_tokens,
+                                             early_tables=self.early_tables)
             mark("attention")
             attn = attn.reshape(B, 1, self.hq * cfg.head_dim)
             partial = self._linear(attn, L["wo"], "o")

@@ -157,17 +157,20 @@ class PagedKVLayerCache:
     def rope_append_decode(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                            rope: RopeTable, out: torch.Tensor | None = None,
                            q_out: torch.Tensor | None = None,
-                           partition_tokens: int | None = None) -> torch.Tensor:
+                           partition_tokens: int | None = None,
+                           early_tables: bool = False) -> torch.Tensor:
         """The whole decode-attention step of the new token: RoPE on q/k, page append
         and paged attention over the grown context, fused into one decode kernel (plus
-        the merge).  Same results as ``append_rotary`` followed by ``decode``."""
+        the merge).  Same results as ``append_rotary`` followed by ``decode``.
+        ``early_tables``: see ``kernels.decode_attention.rope_append_decode``."""
         seq = self._check_kv(k, v)
         if seq != 1:
             raise ValueError("rope_append_decode takes one new token per sequence")
         res = rope_append_decode(q, k, v, self.key_pages, self.value_pages, self.block_table,
                                  self.seq_lens, rope.cos, rope.sin, host_lens=self.host_lengths,
                                  partition_tokens=partition_tokens, out=out, q_out=q_out,
-                                 workspace=self.workspace, status=self.status)
+                                 workspace=self.workspace, status=self.status,
+                                 early_tables=early_tables)
         self.host_lengths = [x + 1 for x in self.host_lengths]
         return res
 

@@ -1,4 +1,5 @@
-"""Fused NVLink all-reduce + residual add + RMSNorm on 2 GPUs (skipped with fewer).
+"""Fused NVLink all-reduce + residual add + RMSNorm on 2 and 4 GPUs (skipped with fewer),
+both algorithms (one-shot and two-shot).
 
 Each rank runs in its own process on its own GPU (NCCL process group for the handle
 exchange and for the reference all-gather).  Checked against an fp32 reference built
@@ -37,8 +38,10 @@ def _reference(partials, x, w, eps):
     return xn, h
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, algo):
     import torch.distributed as dist
+
+    os.environ["LLMC_AR_ALGO"] = algo      # read once, at the first call in this process
 
     from llm_cuda_b200.kernels.allreduce import NvlinkAllReduce
 
@@ -98,13 +101,16 @@ def _worker(rank, world, port, q):
         dist.barrier()
         ar.close()
 
-        # TP2 decode model: fused NVLink path vs NCCL path, same weights and tokens
+        # TP decode model: fused NVLink path vs NCCL path, same weights and tokens
         from llm_cuda_b200.models.llama3.decode_model import (
             DecodeConfig, Llama3DecodeModel, TensorParallel)
 
         cfg = DecodeConfig(vocab_size=1024, hidden_size=1024, intermediate_size=2048,
                            num_hidden_layers=2, num_attention_heads=16, num_key_value_heads=8)
-        logits = []
+        # Greedy ids of the NCCL run are fed to both runs (teacher forcing): a last-bit
+        # difference that flips one argmax would otherwise make every later step of the
+        # two runs decode different tokens.
+        logits, fed = [], []
         for fused in (False, True):
             m = Llama3DecodeModel.random_init(cfg, dev, torch.bfloat16, seed=3,
                                               tp=TensorParallel(rank, world), max_positions=256)
@@ -115,7 +121,11 @@ def _worker(rank, world, port, q):
             with torch.no_grad():
                 nxt = m.prefill(ids, cache).argmax(-1)
                 steps = []
-                for _ in range(4):
+                for t in range(4):
+                    if fused:
+                        nxt = fed[t]
+                    else:
+                        fed.append(nxt.clone())
                     lg = m.decode_step(nxt, cache)
                     steps.append(lg.float().cpu())
                     nxt = lg.argmax(-1)
@@ -132,19 +142,22 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_allreduce_add_rmsnorm_two_ranks():
+@pytest.mark.parametrize("world,algo", [(2, "one_shot"), (2, "two_shot"), (4, "one_shot"),
+                                        (4, "two_shot")])
+def test_fused_allreduce_add_rmsnorm(world, algo):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, algo)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank in (0, 1):
+    for rank in range(world):
         for exact, err in res[rank]["kernel"]:
             assert exact
             assert err <= 2e-2

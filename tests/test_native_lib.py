@@ -114,9 +114,15 @@ def test_host_validation_of_step_entry_points():
                                         1e-5, N.LLMC_BF16, nul)
     assert rc == -1 and b"aligned" in lib.llmc_last_error_string()
     fb = ctypes.c_size_t(0)
-    # two parities x 2 ranks x 64 rows of 8-byte words, each carrying 4 bytes of a row
-    assert lib.llmc_ar_region_bytes(2, 64, 4096, N.LLMC_BF16, ctypes.byref(fb)) == \
-        2 * 2 * 64 * (4096 * 2 // 4) * 8
+    # 8-byte words, each carrying 4 bytes of a row: the larger of the one-shot layout
+    # (2 parities x world x rows) and the two-shot one (reduce-scatter slices plus
+    # all-gather slices with one extra word each)
+    w = 4096 * 2 // 4
+    for world in (2, 4, 8):
+        one = 2 * world * 64 * w
+        two = 2 * 64 * w + 2 * world * 64 * (w // world + 1)
+        assert lib.llmc_ar_region_bytes(world, 64, 4096, N.LLMC_BF16, ctypes.byref(fb)) == \
+            max(one, two) * 8
     assert fb.value == 0
     # argmax
     assert lib.llmc_argmax(1, 1, 70000, 10, N.LLMC_BF16, 8, nul) == -1
@@ -124,7 +130,8 @@ def test_host_validation_of_step_entry_points():
     assert lib.llmc_argmax_workspace_bytes(64) == 64 * 12
     # strided fused step: a sequence stride smaller than the dense one
     args = [1] * 10 + [128] + [1] * 5 + [4, 32, 8, 128, 16, 16, 1024, 0]
-    rc = lib.llmc_rope_append_decode_strided(*args, 0.1, N.LLMC_BF16, 32 * 128 - 1, 8 * 128, nul)
+    rc = lib.llmc_rope_append_decode_strided(*args, 0.1, N.LLMC_BF16, 32 * 128 - 1, 8 * 128, 0,
+                                             nul)
     assert rc == -1 and b"stride" in lib.llmc_last_error_string()
     # decode GEMM shapes
     assert lib.llmc_decode_gemm(1, 1, 1, 1, 4, 1, 64, 100, 64, 1, nul) == -2
