@@ -766,6 +766,31 @@ class PhaseTimer:
         return out, total
 
 
+def _agree(ok: bool, world: int) -> bool:
+    """True when every rank reports ok (a collective: call it on every rank)."""
+    if world == 1:
+        return ok
+    import torch.distributed as dist
+
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def _status_word(model, cache) -> int:
+    """OR of the step's device status words (attention and fused all-reduce); read
+    without raising, then cleared."""
+    torch.cuda.synchronize()
+    words = [cache.layer_caches[0].status]
+    if model.tp.fused is not None:
+        words.append(model.tp.fused.status)
+    w = 0
+    for t in words:
+        w |= int(t.item())
+        t.zero_()
+    return w
+
+
 def measure_c5(world: int, rank: int, dev, steps: int = 128, warmup: int = 5,
                parity_steps: int = 8, variants=("fused", "nccl"), tc_gemms=None,
                with_e2e: bool = True) -> dict:
@@ -833,8 +858,17 @@ def measure_c5(world: int, rank: int, dev, steps: int = 128, warmup: int = 5,
         for _ in range(max(3, warmup)):
             graph.replay()
         reset(graph)
-        torch.cuda.synchronize()
-        model.check_status(cache)
+        word = _status_word(model, cache)
+        if not _agree(word == 0, world):
+            # Every rank leaves this variant together (a device wait timed out on some
+            # rank); the status word is reported, the next variant runs without it.
+            out[variant] = {"error": f"device status {word:#x} on rank {rank} in warm-up"}
+            record = None
+            del graph
+            torch.cuda.synchronize()
+            if variant == "fused":
+                fused_ar = None
+            continue
         _barrier(world)
         clock = ClockSampler(dev.index if world > 1 else 0)
         with clock:
@@ -850,23 +884,33 @@ def measure_c5(world: int, rank: int, dev, steps: int = 128, warmup: int = 5,
             torch.cuda.synchronize()
             _barrier(world)
         clocks.append(clock.summary())
-        model.check_status(cache)
+        word = _status_word(model, cache)
         ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world)
-        out[variant] = {"tokens_per_s": B / (ms * 1e-3), "ms_per_step": ms,
-                        "hbm_gbs_per_gpu": bytes_rank / (ms * 1e-3) / 1e9,
-                        "hbm_frac_per_gpu": bytes_rank / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]}
+        if not _agree(word == 0, world):
+            out[variant] = {"error": f"device status {word:#x} on rank {rank} while timed"}
+            if variant == "fused":
+                fused_ar, record = None, None
+        else:
+            out[variant] = {"tokens_per_s": B / (ms * 1e-3), "ms_per_step": ms,
+                            "hbm_gbs_per_gpu": bytes_rank / (ms * 1e-3) / 1e9,
+                            "hbm_frac_per_gpu": bytes_rank / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"]}
         # The step graph may hold captured NCCL all-reduces: release it before the next.
         del graph
         torch.cuda.synchronize()
-    best = "fused" if world == 1 else max(("fused", "nccl"), key=lambda v: out[v]["tokens_per_s"])
-    out["tokens_per_s"] = out["fused"]["tokens_per_s"]
-    out["ms_per_step"] = out["fused"]["ms_per_step"]
-    out["hbm_frac_per_gpu"] = out["fused"]["hbm_frac_per_gpu"]
-    out["faster_allreduce"] = best if world > 1 else "none (TP1)"
+    good = [v for v in ("fused", "nccl") if "tokens_per_s" in out.get(v, {})]
+    if not good:
+        raise RuntimeError(f"config 5: no variant completed: {out}")
+    main_v = "fused" if "fused" in good else good[0]
+    out["tokens_per_s"] = out[main_v]["tokens_per_s"]
+    out["ms_per_step"] = out[main_v]["ms_per_step"]
+    out["hbm_frac_per_gpu"] = out[main_v]["hbm_frac_per_gpu"]
+    out["reported_variant"] = main_v
+    out["faster_allreduce"] = (max(good, key=lambda v: out[v]["tokens_per_s"]) if world > 1
+                               else "none (TP1)")
     out["roofline_ms_per_step"] = bytes_rank / (peaks["hbm_gbs"] * 1e9) * 1e3
 
-    # ---- per-phase split of one step (fused variant): timing event nodes between the
-    # phases of an instrumented copy of the graph ----
+    # ---- per-phase split of one step (the reported variant): timing event nodes
+    # between the phases of an instrumented copy of the graph ----
     model.tp.fused = fused_ar
     timer = PhaseTimer()
     model.mark = timer
@@ -890,8 +934,9 @@ def measure_c5(world: int, rank: int, dev, steps: int = 128, warmup: int = 5,
         out["split_ms"] = {"unavailable": f"{type(ex).__name__}: {str(ex)[:160]}"}
     finally:
         model.mark = None
-    torch.cuda.synchronize()
-    model.check_status(cache)
+    word = _status_word(model, cache)
+    if not _agree(word == 0, world):
+        out["split_ms"] = {"unavailable": f"device status {word:#x} on rank {rank}"}
 
     # ---- e2e: host ids in (pinned), greedy ids out, eager public API per step ----
     if with_e2e:
@@ -916,7 +961,9 @@ def measure_c5(world: int, rank: int, dev, steps: int = 128, warmup: int = 5,
         out["e2e"] = {"value": B / (e2e_ms * 1e-3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                       "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
                       "path": "Llama3DecodeModel.decode_step eager + argmax, host ids in/out"}
-    model.check_status(cache)
+        word = _status_word(model, cache)
+        if not _agree(word == 0, world):
+            out["e2e"] = {"error": f"device status {word:#x} on rank {rank}"}
 
     # ---- TP=N against TP1 (rank 0): same weights, same prompt, teacher-forced ids ----
     if record is not None:
@@ -973,7 +1020,9 @@ def run_c5_main(args):
                    tc_gemms=args.tc_gemms,
                    variants=("nccl", "fused") if args.nccl_allreduce else ("fused", "nccl"))
     if rank == 0:
-        main_v = "nccl" if (args.nccl_allreduce and world > 1) else "fused"
+        main_v = r["reported_variant"]
+        if args.nccl_allreduce and world > 1 and "tokens_per_s" in r.get("nccl", {}):
+            main_v = "nccl"
         line = {
             "metric": "decode tokens/s (config 5 full decode step)",
             "value": r[main_v]["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,

@@ -330,8 +330,9 @@ LLMC_API int llmc_argmax(const void* x, int64_t* out, int rows, int n, int dtype
  * that carry 4 bytes of data and the call's epoch, and polls, bounded at 2 s, until
  * every peer's words of this epoch have arrived (no fence, no separate flag). On
  * timeout LLMC_STATUS_WAIT_TIMEOUT is set, the row is left unchanged and the row's
- * epoch still advances. The ranks' epochs may then be out of step, so stop using the
- * regions and rebuild them. Calls must be issued in the same order on all ranks.
+ * epoch still advances. The ranks' epochs may then be out of step: while the status
+ * word holds that bit, calls return at once and leave their rows unchanged; stop using
+ * the regions and rebuild them. Calls must be issued in the same order on all ranks.
  */
 LLMC_API size_t llmc_ipc_handle_bytes(void);
 LLMC_API int llmc_ipc_alloc(size_t bytes, void** dev_ptr, void* handle);

@@ -67,9 +67,15 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_kernel(const Param
 
   if (threadIdx.x == 0) {
     s_epoch = p.epoch[b] + 1;
-    s_fail = 0;
+    // After a timeout the ranks' epochs may be out of step: later calls (e.g. replays
+    // of a captured graph) fail at once instead of each waiting out the deadline.
+    s_fail = (*reinterpret_cast<volatile int32_t*>(p.status) & kStatusWaitTimeout) ? 1 : 0;
   }
   __syncthreads();
+  if (s_fail) {
+    if (threadIdx.x == 0) p.epoch[b] = s_epoch;
+    return;
+  }
   const uint32_t e = (uint32_t)s_epoch;
   const int par = e & 1;
   const size_t row_words = (size_t)nvec * 4;                       // 8-byte words per row
@@ -226,9 +232,15 @@ __global__ void __launch_bounds__(1024) allreduce_add_rmsnorm_2shot_kernel(const
 
   if (threadIdx.x == 0) {
     s_epoch = p.epoch[b] + 1;
-    s_fail = 0;
+    // After a timeout the ranks' epochs may be out of step: later calls (e.g. replays
+    // of a captured graph) fail at once instead of each waiting out the deadline.
+    s_fail = (*reinterpret_cast<volatile int32_t*>(p.status) & kStatusWaitTimeout) ? 1 : 0;
   }
   __syncthreads();
+  if (s_fail) {
+    if (threadIdx.x == 0) p.epoch[b] = s_epoch;
+    return;
+  }
   const uint32_t e = (uint32_t)s_epoch;
   const int par = e & 1;
   const size_t rs_par = (size_t)p.world * p.rows_cap * sw;           // RS words per parity
