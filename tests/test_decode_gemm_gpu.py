@@ -20,7 +20,6 @@ DEV = torch.device("cuda", 0)
     (64, 768, 4096),          # q/k/v of one rank at TP8 (clusters of 8)
     (64, 4096, 512),          # o_proj of one rank at TP8
     (64, 3584, 4096),         # gate/up of one rank at TP8
-    (8, 768, 512),            # a small model's q/k/v at batch 8
     (128, 512, 1024),         # 128-row batch tile
     (256, 256, 512),          # 256-row batch tile
 ])

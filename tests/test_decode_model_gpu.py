@@ -212,7 +212,7 @@ def test_early_tables_step_equals_ordered_step():
                        num_hidden_layers=3, num_attention_heads=8, num_key_value_heads=2)
     m = Llama3DecodeModel.random_init(cfg, DEV, torch.bfloat16, seed=11, max_positions=512)
     m.tc_projections = {"qkv", "o", "gate_up", "down"}     # PDL-aware GEMMs before attention
-    B, S, steps = 8, 300, 4
+    B, S, steps = 64, 300, 4
     ids = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(3)).to(DEV)
 
     def run(early: bool, graph: bool):
