@@ -588,11 +588,13 @@ def measure_decode(name: str, w: dict, lengths, steps: int, warmup: int, world: 
         e1 = torch.cuda.Event(enable_timing=True)
         _barrier(world)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_steps")
         with torch.cuda.stream(stream):
             e0.record(stream)
             for i in range(steps):
                 graphs[i % n_sets].replay()
             e1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         _barrier(world)
         ms = e0.elapsed_time(e1) / steps
@@ -877,10 +879,12 @@ def measure_c5(world: int, rank: int, dev, steps: int = 128, warmup: int = 5,
             _barrier(world)
             torch.cuda.synchronize()
             stream = torch.cuda.current_stream(dev)
+            torch.cuda.nvtx.range_push(f"c5_steps_{variant}")
             e0.record(stream)
             for _ in range(steps):
                 graph.replay()
             e1.record(stream)
+            torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()
             _barrier(world)
         clocks.append(clock.summary())
