@@ -1428,7 +1428,7 @@ static void set_split(fast::Params& p, int Tpart, float* part_o, float* part_lse
     p.counters = nullptr;
     p.part_lse = part_lse;
     p.T = Tpart;
-    p.max_parts = (p.max_pages * p.P + Tpart - 1) / Tpart;
+    p.max_parts = (int)(((long long)p.max_pages * p.P + Tpart - 1) / Tpart);
   }
 }
 
