@@ -1,4 +1,4 @@
-"""Multi-rank host logic of the TP decode step on CPU ``gloo`` ranks (world size 2).
+"""Multi-rank host logic of the TP decode step on CPU ``gloo`` ranks (world size 2 and 4).
 
 The CUDA kernels need a GPU, so the attention core is replaced by a dense torch
 restatement of the reference's decode branch (RoPE, cache concat, repeat_kv,
@@ -11,6 +11,7 @@ import datetime
 import os
 import socket
 
+import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
@@ -95,7 +96,8 @@ def _worker(rank, world, port, ids, q):
         dist.destroy_process_group()
 
 
-def test_tp2_decode_matches_tp1_on_gloo():
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_decode_matches_tp1_on_gloo(world):
     torch.manual_seed(0)
     ids = torch.randint(0, CFG.vocab_size, (3, 6))
     ref = _run(Llama3DecodeModel.random_init(CFG, "cpu", torch.float32, seed=3, max_positions=64),
@@ -103,7 +105,7 @@ def test_tp2_decode_matches_tp1_on_gloo():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, ids, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, ids, q)) for r in range(world)]
     for p in procs:
         p.start()
     out = q.get(timeout=120)
