@@ -18,6 +18,7 @@ _LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "li
 LLMC_F32, LLMC_F16, LLMC_BF16 = 0, 1, 2
 LLMC_DECODE_FORCE_GENERIC = 1
 LLMC_DECODE_EARLY_TABLES = 2
+LLMC_STATUS_WAIT_TIMEOUT = 1
 
 STATUS_BITS = {
     1: "pipeline wait timeout",

@@ -101,6 +101,9 @@ class NvlinkAllReduce:
             N.raise_on_status(self.status)
         except N.DeviceStatusError:
             self.failed = True
+            # Keep the timeout bit set: kernels already captured in a graph then return
+            # at once on replay instead of each waiting out the deadline.
+            self.status.fill_(N.LLMC_STATUS_WAIT_TIMEOUT)
             raise
 
     def close(self) -> None:
