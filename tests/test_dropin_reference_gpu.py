@@ -48,7 +48,7 @@ def ref_model(monkeypatch):
     from llm_cuda_b200.kernels import decode_attention as ours
     from llm_cuda_b200.models.llama3 import kv_cache as our_cache
 
-    # the swap a user makes: decode attention + paged cache
+    # the swap a user makes: decode attention + paged cache, rebound in the reference's modules
     monkeypatch.setattr(ref_attention, "can_use_triton_decode_attention",
                         ours.can_use_triton_decode_attention)
     monkeypatch.setattr(ref_attention, "triton_decode_attention", ours.triton_decode_attention)
