@@ -477,7 +477,10 @@ def _balanced_partials(lengths, hkv: int, group: int, grid: int) -> int:
     n, x0 = 0, 0
     for c, h in zip(chunks, heads):
         if c:
-            segs = owner(x0 + c - 1) - owner(x0) + 1
+            if total >= grid:   # every CTA owns a chunk: the owners are consecutive
+                segs = owner(x0 + c - 1) - owner(x0) + 1
+            else:               # some CTAs own nothing and hold no segment
+                segs = len({owner(x) for x in range(x0, x0 + c)})
             if segs > 1:
                 n += segs * h
         x0 += c
