@@ -13,13 +13,14 @@ The caller of the decode-attention path: one decode step of a Llama-3 model
   reference's layout (``parallel/tensor_parallel.py:8-90``): q/k/v/gate/up are
   column-split (rank i owns output rows ``[i*o/N, (i+1)*o/N)``, i.e. whole query
   and KV heads), o_proj/down_proj are row-split (input columns), and the
-  reference's in-process sum of row-parallel partials (:83-90) is an NCCL
-  all-reduce over NVLink.  Embedding and lm_head are replicated (the reference
-  does not shard them, model.py:50,115);
+  reference's in-process sum of row-parallel partials (:83-90) is an all-reduce
+  over NVLink: this package's fused kernel (``enable_fused_allreduce``: one launch
+  that also does the residual add + RMSNorm, one- or two-shot over peer memory) or
+  NCCL.  Embedding and lm_head are replicated (the reference does not shard them,
+  model.py:50,115);
 * residual add + RMSNorm (``norm.py:31-33``), SwiGLU (``kernels/triton/swiglu.py:103-107``)
-  and the greedy argmax as CUDA kernels of this package; at TP > 1 the all-reduce of
-  the row-parallel partials can be the fused one-shot NVLink kernel that also does the
-  add + RMSNorm; dense projections on cuBLAS or the tcgen05 decode GEMM.
+  and the greedy argmax as CUDA kernels of this package; dense projections on cuBLAS
+  or the tcgen05 decode GEMM (``tc_projections``).
 
 ``decode_step`` allocates nothing and reads lengths on the device, so the whole
 step (all layers, all-reduces, lm_head, greedy argmax) is captured once in a
