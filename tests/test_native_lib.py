@@ -37,6 +37,27 @@ def test_library_exports_every_declared_symbol():
     assert b"sm_100a" in lib.llmc_version()
 
 
+def _declared_param_counts():
+    counts = {}
+    inc = os.path.join(ROOT, "include")
+    for f in os.listdir(inc):
+        if f.endswith(".h"):
+            src = open(os.path.join(inc, f)).read()
+            for name, params in re.findall(r"LLMC_API\s+[\w\s\*]+?\b(llmc_\w+)\s*\(([^)]*)\)",
+                                           src):
+                params = params.strip()
+                counts[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return counts
+
+
+def test_ctypes_signatures_match_header():
+    """Every ctypes prototype has as many arguments as the header's declaration."""
+    counts = _declared_param_counts()
+    assert counts
+    for name, n in counts.items():
+        assert len(N.SIGNATURES[name][1]) == n, (name, len(N.SIGNATURES[name][1]), n)
+
+
 def test_host_validation_without_gpu():
     lib = N.load()
     nul = None
